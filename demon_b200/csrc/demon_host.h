@@ -1,0 +1,51 @@
+// demon_host.h -- host-side helpers shared by the C-ABI entry points:
+// thread-local error message, argument checks, CUDA error mapping, device
+// capability check, and TMA tensor-map encoding through the driver entry point.
+#pragma once
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace demon {
+
+void set_error(const char* fmt, ...);
+int check_device();  // DEMON_OK if the current device is sm_100, else DEMON_ERR_UNSUPPORTED/CUDA
+unsigned int* status_word();  // device address of the per-device status word (nullptr on failure)
+
+// True until mark_device_done(flags) ran on the current device (per-device once-flags
+// for function attributes, which the runtime keeps per device).
+bool device_pending(const std::atomic<uint64_t>& flags);
+void mark_device_done(std::atomic<uint64_t>& flags);
+
+// 2-D row-major tiled tensor map: `rows` x `cols` elements of `elem_bytes`,
+// row pitch `ld_bytes`, box `box_rows` x `box_cols`, 128-byte swizzle.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
+                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows);
+
+}  // namespace demon
+
+#define DEMON_API_BEGIN()                   \
+  do {                                      \
+    int _dev_rc = ::demon::check_device();  \
+    if (_dev_rc != DEMON_OK) return _dev_rc; \
+  } while (0)
+
+#define DEMON_CHECK_ARG(cond, ...)      \
+  do {                                  \
+    if (!(cond)) {                      \
+      ::demon::set_error(__VA_ARGS__);  \
+      return DEMON_ERR_INVALID;         \
+    }                                   \
+  } while (0)
+
+#define DEMON_CUDA(call)                                                               \
+  do {                                                                                 \
+    cudaError_t _e = (call);                                                           \
+    if (_e != cudaSuccess) {                                                           \
+      ::demon::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__, __LINE__); \
+      return DEMON_ERR_CUDA;                                                           \
+    }                                                                                  \
+  } while (0)

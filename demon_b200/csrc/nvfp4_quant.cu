@@ -1,0 +1,215 @@
+// nvfp4_quant.cu -- NVFP4 activation quantiser for sm_100a.
+//
+// bf16 [M, K] -> E2M1 codes [M, K/2] + E4M3 block scales (16 elements along K,
+// tcgen05 128x4-chunk layout) + fp32 global scale(s).
+//
+// Arithmetic, step by step (identical to the CPU restatement the tests check
+// against; every step is one IEEE binary32 round-to-nearest-even operation):
+//   g     = max(amax, 1e-12) / 2688                 (per row, per tensor or given)
+//   s_b   = e4m3_rne(min(amax_b / (6 g), 448))       clamp before the cast, as the
+//                                                   reference's FP8 re-quantiser does
+//                                                   (acestep/engine/trt/lora_refit.py:598-601)
+//   code  = e2m1_rne(x * (1 / (f32(s_b) * g)))      saturating at 6, zero -> code 0
+// The absmax floor 1e-12 is the reference's FP8 floor (acestep/engine/trt/fp8_onnx.py:67).
+//
+// Layout of the work: one warp per row.  Lane l owns the 8-element chunks
+// l + 32 j (one 128-bit load each), so lanes (2i, 2i+1) hold one 16-element
+// block; the block absmax is one shuffle.  Codes of a chunk are one 32-bit
+// store (a warp writes 128 contiguous bytes); four block scales that are
+// contiguous in the scale layout are gathered by shuffles into one 32-bit store.
+#include <algorithm>
+#include <cuda_fp8.h>
+
+#include "demon_common.cuh"
+#include "demon_host.h"
+
+namespace demon {
+
+__device__ __forceinline__ uint32_t e2m1_code(float v) {
+  const float a = fabsf(v);
+  uint32_t mag;
+  if (!(a > 0.25f)) mag = 0;
+  else if (a < 0.75f) mag = 1;
+  else if (a <= 1.25f) mag = 2;
+  else if (a < 1.75f) mag = 3;
+  else if (a <= 2.5f) mag = 4;
+  else if (a < 3.5f) mag = 5;
+  else if (a <= 5.0f) mag = 6;
+  else mag = 7;
+  return (mag != 0u && v < 0.0f) ? (mag | 8u) : mag;
+}
+
+// E4M3FN byte -> float (format definition: bias 7, subnormals m * 2^-9).
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+  const uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+  const float v = (e == 0u) ? __int2float_rn((int)m) * 0.001953125f
+                            : __int2float_rn((int)(8u + m)) * __uint_as_float((e + 117u) << 23);  // 2^(e-10)
+  return (b & 0x80u) ? -v : v;
+}
+
+__device__ __forceinline__ uint32_t e4m3_rne_sat(float s) {
+  return (uint32_t)__nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ float global_scale(float amax) {
+  return __fdiv_rn(fmaxf(amax, 1e-12f), 2688.0f);
+}
+
+__device__ __forceinline__ float amax8(uint4 v) {
+  float a = fabsf(bf16_lo(v.x));
+  a = fmaxf(a, fabsf(bf16_hi(v.x)));
+  a = fmaxf(a, fabsf(bf16_lo(v.y)));
+  a = fmaxf(a, fabsf(bf16_hi(v.y)));
+  a = fmaxf(a, fabsf(bf16_lo(v.z)));
+  a = fmaxf(a, fabsf(bf16_hi(v.z)));
+  a = fmaxf(a, fabsf(bf16_lo(v.w)));
+  a = fmaxf(a, fabsf(bf16_hi(v.w)));
+  return a;
+}
+
+__device__ __forceinline__ uint32_t pack8(uint4 v, float rs) {
+  uint32_t c = 0;
+  c |= e2m1_code(__fmul_rn(bf16_lo(v.x), rs)) << 0;
+  c |= e2m1_code(__fmul_rn(bf16_hi(v.x), rs)) << 4;
+  c |= e2m1_code(__fmul_rn(bf16_lo(v.y), rs)) << 8;
+  c |= e2m1_code(__fmul_rn(bf16_hi(v.y), rs)) << 12;
+  c |= e2m1_code(__fmul_rn(bf16_lo(v.z), rs)) << 16;
+  c |= e2m1_code(__fmul_rn(bf16_hi(v.z), rs)) << 20;
+  c |= e2m1_code(__fmul_rn(bf16_lo(v.w), rs)) << 24;
+  c |= e2m1_code(__fmul_rn(bf16_hi(v.w), rs)) << 28;
+  return c;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+constexpr int kQuantWarps = 8;
+
+// Row absmax over the whole tensor -> atomicMax on the float bits in *amax_out
+// (valid because every candidate is a non-negative float).
+__global__ void __launch_bounds__(256) amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
+                                                   int64_t ldx, float* amax_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kQuantWarps;
+  float a = 0.0f;
+  for (int64_t m = warp; m < M; m += nwarps) {
+    const uint4* row = reinterpret_cast<const uint4*>(x + m * ldx);
+    for (int64_t c = lane; c < K / 8; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
+  }
+  a = warp_max(a);
+  __shared__ float red[kQuantWarps];
+  if (lane == 0) red[threadIdx.x >> 5] = a;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = red[0];
+    for (int i = 1; i < kQuantWarps; ++i) b = fmaxf(b, red[i]);
+    atomicMax(reinterpret_cast<int*>(amax_out), __float_as_int(b));
+  }
+}
+
+__global__ void finalize_gs_kernel(float* gs) { gs[0] = global_scale(gs[0]); }
+
+// GS_MODE: 0 static (gs[0] is g), 1 dynamic (gs[0] holds amax, g derived), 2 per row.
+template <int GS_MODE>
+__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
+                                                       int64_t ldx, int64_t Mpad, float* __restrict__ gs,
+                                                       uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  const int lane = threadIdx.x & 31;
+  const int64_t m = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
+  if (m >= Mpad) return;
+  const int64_t nchunk = K / 8;      // 8-element chunks per row
+  const int64_t kchunks64 = K / 64;  // scale chunks per 128-row block
+  const int64_t r = m & 127;
+  uint8_t* sf_rowbase = sf + (m >> 7) * kchunks64 * 512 + (r & 31) * 16 + (r >> 5) * 4;
+
+  if (m >= M) {  // padding rows of the scale layout: zero scales
+    for (int64_t c = lane; c < K / 64; c += 32) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+    return;
+  }
+  const uint4* row = reinterpret_cast<const uint4*>(x + m * ldx);
+
+  float g;
+  if (GS_MODE == 0) {
+    g = gs[0];
+  } else if (GS_MODE == 1) {
+    g = global_scale(gs[0]);
+  } else {
+    float a = 0.0f;
+    for (int64_t c = lane; c < nchunk; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
+    g = global_scale(warp_max(a));
+    if (lane == 0) gs[m] = g;
+  }
+  const float denom = __fmul_rn(6.0f, g);
+  uint32_t* code_row = reinterpret_cast<uint32_t*>(codes + m * (K / 2));
+
+  // Every lane runs every iteration (shuffles need the full warp); K % 64 == 0
+  // makes the valid lanes of the last iteration whole groups of 8.
+  for (int64_t base = 0; base < nchunk; base += 32) {
+    const int64_t c = base + lane;
+    const bool valid = c < nchunk;
+    const uint4 v = valid ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
+    const float mine = amax8(v);
+    const float am = fmaxf(mine, __shfl_xor_sync(0xffffffffu, mine, 1));
+    const float s = fminf(__fdiv_rn(am, denom), 448.0f);
+    const uint32_t sb = e4m3_rne_sat(s);
+    const float sbf = e4m3_value(sb);
+    uint32_t packed = 0u;
+    if (sbf != 0.0f) packed = pack8(v, __frcp_rn(__fmul_rn(sbf, g)));
+    // block kb = c / 2; lanes with lane % 8 == 0 gather the scales of blocks kb..kb+3
+    const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
+    const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
+    const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
+    if (valid) {
+      code_row[c] = packed;
+      if ((lane & 7) == 0) {
+        const int64_t kb = c >> 1;
+        *reinterpret_cast<uint32_t*>(sf_rowbase + (kb >> 2) * 512) = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+      }
+    }
+  }
+}
+
+}  // namespace demon
+
+using namespace demon;
+
+extern "C" int64_t demon_nvfp4_sf_bytes(int64_t rows, int64_t K) {
+  if (rows < 0 || K < 0) return -1;
+  return ((rows + 127) / 128) * 128 * (K / 16);
+}
+
+extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, float* gs,
+                                    uint8_t* codes, uint8_t* sf, void* stream) {
+  DEMON_API_BEGIN();
+  DEMON_CHECK_ARG(M >= 0 && K > 0 && K % 64 == 0, "quantize: need K > 0, K %% 64 == 0 (K=%lld)", (long long)K);
+  DEMON_CHECK_ARG(ldx >= K && ldx % 8 == 0, "quantize: ldx must be >= K and a multiple of 8 (ldx=%lld)",
+                  (long long)ldx);
+  DEMON_CHECK_ARG(gs_mode >= 0 && gs_mode <= 2, "quantize: bad gs_mode %d", gs_mode);
+  DEMON_CHECK_ARG(gs != nullptr && (M == 0 || (x && codes && sf)), "quantize: null pointer");
+  DEMON_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 3) == 0 && ((uintptr_t)sf & 3) == 0,
+                  "quantize: x must be 16-byte aligned, codes/sf 4-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t Mpad = (M + 127) / 128 * 128;
+  if (Mpad == 0) return DEMON_OK;
+  const dim3 grid((unsigned)((Mpad + kQuantWarps - 1) / kQuantWarps));
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  if (gs_mode == DEMON_GS_STATIC) {
+    quantize_kernel<0><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+  } else if (gs_mode == DEMON_GS_DYNAMIC) {
+    DEMON_CUDA(cudaMemsetAsync(gs, 0, sizeof(float), st));
+    if (M > 0) {
+      const int blocks = (int)std::min<int64_t>((M + kQuantWarps - 1) / kQuantWarps, 148 * 8);
+      amax_kernel<<<blocks, 256, 0, st>>>(xb, M, K, ldx, gs);
+    }
+    quantize_kernel<1><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+    finalize_gs_kernel<<<1, 1, 0, st>>>(gs);
+  } else {
+    quantize_kernel<2><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+  }
+  DEMON_CUDA(cudaGetLastError());
+  return DEMON_OK;
+}

@@ -1,0 +1,247 @@
+"""NVFP4 quantised linear: host side of the quantiser / GEMM / LoRA C ABI.
+
+Drop-in for the DiT ``nn.Linear`` call sites of the reference
+(acestep/models/modeling_acestep_v15_turbo.py:286-289 q/k/v/o, :34-35 and :538
+the Qwen3 MLP gate/up/down): :class:`NVFP4Linear` keeps ``forward(x)`` with
+``x [..., K] bf16 -> [..., N] bf16`` and the ``weight`` / ``bias`` state-dict
+names, and adds the fused gated-residual epilogue used after ``o_proj`` and
+the MLP (turbo.py:525-546) plus a hot LoRA whose strength is a kernel scalar
+(the reference's LoRA contract, acestep/engine/lora.py:383-526, without the
+weight rewrite of lora.py:811-833).
+
+Every call goes through ``libdemon_b200.so``; there is no PyTorch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native as nat
+
+
+@dataclass
+class NVFP4Tensor:
+    """Packed NVFP4 operand: E2M1 codes, tcgen05-layout E4M3 block scales, fp32 global scale(s)."""
+    codes: torch.Tensor   # uint8 [rows, K/2]
+    sf: torch.Tensor      # uint8 [sf_bytes(rows, K)]
+    gs: torch.Tensor      # float32 [1] or [rows]
+    rows: int
+    K: int
+    per_row: bool = False  # gs holds one scale per row
+
+
+def _check_cuda_bf16(x: torch.Tensor, name: str) -> None:
+    if not x.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (demon_b200 has no CPU path)")
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16, got {x.dtype}")
+
+
+def quantize(x: torch.Tensor, gs_mode: int = nat.GS_PER_ROW, gs: torch.Tensor | None = None,
+             stream=None) -> NVFP4Tensor:
+    """Quantise bf16 ``x [M, K]`` (row stride may exceed K) to NVFP4.
+
+    ``gs_mode``: GS_PER_ROW (default; one global scale per row, so a row's
+    codes never depend on the rest of the batch), GS_DYNAMIC (one scale from
+    the tensor absmax) or GS_STATIC (``gs`` given, float32 [1]).
+    """
+    _check_cuda_bf16(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("quantize expects a 2-D tensor with unit stride along K")
+    M, K = x.shape
+    dev = x.device
+    codes = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+    sf = torch.empty((nat.sf_bytes(M, K),), dtype=torch.uint8, device=dev)
+    if gs_mode == nat.GS_STATIC:
+        if gs is None or gs.dtype != torch.float32 or gs.numel() != 1 or not gs.is_cuda:
+            raise ValueError("GS_STATIC needs gs: float32 [1] CUDA tensor")
+        g = gs
+    else:
+        g = torch.empty((M if gs_mode == nat.GS_PER_ROW else 1,), dtype=torch.float32, device=dev)
+    nat.check(nat.load().demon_nvfp4_quantize(
+        nat.ptr(x), M, K, x.stride(0), gs_mode, nat.ptr(g), nat.ptr(codes), nat.ptr(sf), nat.stream_ptr(stream)))
+    return NVFP4Tensor(codes, sf, g, M, K, per_row=gs_mode == nat.GS_PER_ROW)
+
+
+def pack_weight(w: torch.Tensor, stream=None) -> NVFP4Tensor:
+    """Pack a bf16 weight ``[N, K]`` (torch Linear layout) with one per-tensor global scale.
+
+    Plays the role of the reference's offline weight quantiser
+    (acestep/engine/trt/fp8_onnx.py:115-149) for NVFP4.
+    """
+    return quantize(w.contiguous(), nat.GS_DYNAMIC, stream=stream)
+
+
+def lora_down(x: torch.Tensor, lora_a: torch.Tensor, col_scale: torch.Tensor, a: NVFP4Tensor,
+              w: NVFP4Tensor, stream=None) -> torch.Tensor:
+    """xa = col_scale * (x @ lora_a^T) / (a_gs * w_gs), bf16 [M, r] (tcgen05 bf16 GEMM)."""
+    _check_cuda_bf16(x, "x")
+    _check_cuda_bf16(lora_a, "lora_a")
+    M, K = x.shape
+    r = lora_a.shape[0]
+    xa = torch.empty((M, r), dtype=torch.bfloat16, device=x.device)
+    nat.check(nat.load().demon_lora_down(
+        nat.ptr(x), M, K, x.stride(0), nat.ptr(lora_a.contiguous()), r, nat.ptr(col_scale),
+        nat.ptr(a.gs), int(a.per_row), nat.ptr(w.gs), nat.ptr(xa), nat.stream_ptr(stream)))
+    return xa
+
+
+def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, gate_rows: int = 1,
+         lora_xa: torch.Tensor | None = None, lora_b: torch.Tensor | None = None,
+         out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out = residual + gate * (alpha * (A W^T + lora) + bias), bf16 [M, N]."""
+    if a.K != w.K:
+        raise ValueError(f"K mismatch: activations {a.K} vs weight {w.K}")
+    M, N, K = a.rows, w.rows, a.K
+    dev = a.codes.device
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    args = nat.DemonGemmArgs()
+    args.a_codes, args.a_sf, args.a_gs = nat.ptr(a.codes), nat.ptr(a.sf), nat.ptr(a.gs)
+    args.a_gs_per_row = int(a.per_row)
+    args.w_codes, args.w_sf, args.w_gs = nat.ptr(w.codes), nat.ptr(w.sf), nat.ptr(w.gs)
+    args.M, args.N, args.K = M, N, K
+    args.out, args.ldo = nat.ptr(out), out.stride(0)
+    args.bias = nat.ptr(bias)
+    if residual is not None:
+        args.residual, args.ldr = nat.ptr(residual), residual.stride(0)
+    if gate is not None:
+        args.gate, args.gate_rows, args.ld_gate = nat.ptr(gate), gate_rows, gate.stride(0)
+    if lora_xa is not None:
+        args.lora_xa, args.lora_b, args.lora_rank = nat.ptr(lora_xa), nat.ptr(lora_b), lora_xa.shape[1]
+    nat.check(nat.load().demon_nvfp4_gemm(ctypes.byref(args), nat.stream_ptr(stream)))
+    return out
+
+
+@dataclass
+class _LoRAEntry:
+    A: torch.Tensor          # bf16 [r, K]  (PEFT lora_A)
+    B: torch.Tensor          # bf16 [N, r]  (PEFT lora_B)
+    strength: float = 1.0
+    enabled: bool = True
+
+
+@dataclass
+class LoRABank:
+    """Hot LoRAs of one linear, concatenated along the rank.
+
+    The effective weight is ``W + sum_i s_i B_i A_i`` -- raw ``B @ A`` with no
+    alpha / rank factor, exactly the reference's delta
+    (acestep/engine/lora.py:316-319) and writeback (lora.py:824-833).  The
+    strength of each LoRA is a per-rank-column scale of the down projection,
+    so enable / disable / set_strength never touch the packed weight.
+    """
+    entries: dict = field(default_factory=dict)
+    _cat: tuple | None = None
+
+    def set(self, lora_id: str, A: torch.Tensor, B: torch.Tensor, strength: float = 1.0) -> None:
+        self.entries[lora_id] = _LoRAEntry(A.to(torch.bfloat16).contiguous(), B.to(torch.bfloat16).contiguous(),
+                                           float(strength))
+        self._cat = None
+
+    def remove(self, lora_id: str) -> None:
+        self.entries.pop(lora_id, None)
+        self._cat = None
+
+    def set_strength(self, lora_id: str, strength: float) -> None:
+        self.entries[lora_id].strength = float(strength)
+        self._cat = None
+
+    def enable(self, lora_id: str, enabled: bool = True) -> None:
+        self.entries[lora_id].enabled = enabled
+        self._cat = None
+
+    def active(self):
+        """(A_cat [R, K], B_cat [N, R], col_scale fp32 [R]) or None when no LoRA contributes."""
+        if self._cat is None:
+            live = [e for e in self.entries.values() if e.enabled and e.strength != 0.0]
+            if not live:
+                self._cat = (None,)
+            else:
+                A = torch.cat([e.A for e in live], 0)
+                B = torch.cat([e.B for e in live], 1)
+                scale = torch.cat([torch.full((e.A.shape[0],), e.strength, dtype=torch.float32) for e in live])
+                r = A.shape[0]
+                pad = (-r) % 16
+                if pad:
+                    A = torch.cat([A, A.new_zeros(pad, A.shape[1])], 0)
+                    B = torch.cat([B, B.new_zeros(B.shape[0], pad)], 1)
+                    scale = torch.cat([scale, scale.new_zeros(pad)])
+                if A.shape[0] > 128:
+                    raise ValueError(f"total LoRA rank {A.shape[0]} exceeds 128 for one linear")
+                self._cat = (A.contiguous(), B.contiguous(), scale.to(A.device))
+        return None if self._cat[0] is None else self._cat
+
+
+class NVFP4Linear(torch.nn.Module):
+    """Drop-in for ``nn.Linear`` backed by the NVFP4 quantiser + tcgen05 GEMM.
+
+    ``weight`` (bf16 [N, K]) and ``bias`` keep their ``nn.Linear`` names; the
+    packed operand is rebuilt by :meth:`repack` (done lazily on first forward
+    and after ``load_state_dict``).
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None,
+                 keep_weight: bool = True):
+        super().__init__()
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = torch.nn.Parameter(
+            torch.empty(out_features, in_features, dtype=torch.bfloat16, device=device), requires_grad=False)
+        self.bias = (torch.nn.Parameter(torch.zeros(out_features, dtype=torch.bfloat16, device=device),
+                                        requires_grad=False) if bias else None)
+        self.keep_weight = keep_weight
+        self.packed: NVFP4Tensor | None = None
+        self.lora = LoRABank()
+
+    @classmethod
+    def from_linear(cls, lin: torch.nn.Linear, keep_weight: bool = True) -> "NVFP4Linear":
+        m = cls(lin.in_features, lin.out_features, lin.bias is not None, device=lin.weight.device,
+                keep_weight=keep_weight)
+        with torch.no_grad():
+            m.weight.copy_(lin.weight.to(torch.bfloat16))
+            if lin.bias is not None:
+                m.bias.copy_(lin.bias.to(torch.bfloat16))
+        return m
+
+    def repack(self) -> None:
+        self.packed = pack_weight(self.weight.data)
+        if not self.keep_weight:
+            self.weight.data = torch.empty(0, dtype=torch.bfloat16, device=self.weight.device)
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        super()._load_from_state_dict(*args, **kwargs)
+        self.packed = None
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x W^T + b (+ hot LoRA), then optionally ``residual + gate * y``.
+
+        x: [..., K] bf16.  gate: [B, N] (one row per leading batch index, as the
+        AdaLN gates of the DiT, turbo.py:525-546) or None.  residual: like the output.
+        """
+        if self.packed is None:
+            self.repack()
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        a = quantize(x2)
+        lo = self.lora.active()
+        xa = lb = None
+        if lo is not None:
+            A, B, scale = lo
+            xa = lora_down(x2, A, scale, a, self.packed)
+            lb = B
+        res2 = residual.reshape(-1, self.out_features) if residual is not None else None
+        gate2 = None
+        gate_rows = 1
+        if gate is not None:
+            gate2 = gate.reshape(-1, self.out_features)
+            gate_rows = x2.shape[0] // gate2.shape[0]
+        out2 = out.reshape(-1, self.out_features) if out is not None else None
+        y = gemm(a, self.packed, bias=self.bias, residual=res2, gate=gate2, gate_rows=gate_rows,
+                 lora_xa=xa, lora_b=lb, out=out2)
+        return y.reshape(*lead, self.out_features)

@@ -1,0 +1,215 @@
+/*
+ * demon_b200.h -- C ABI of the B200 (sm_100a) hot path of the DEMON streaming
+ * diffusion engine: NVFP4 quantised linear + fused per-slot ODE step.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers unless the name says host;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - the library never allocates device memory; callers own every buffer;
+ *   - return value 0 = DEMON_OK, otherwise a DEMON_ERR_* code, with a message
+ *     retrievable through demon_last_error() (thread-local);
+ *   - argument errors are detected on the host before any launch;
+ *   - device-side bounded waits that expire set bits in a per-device status
+ *     word, read (and cleared) with demon_device_status().
+ *
+ * The reference has no NVFP4 plugin or op.  Each entry point below names the
+ * reference interface it stands in for (file:line in daydreamlive/DEMON).
+ */
+#ifndef DEMON_B200_H
+#define DEMON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DEMON_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DEMON_API __attribute__((visibility("default")))
+#else
+#define DEMON_API
+#endif
+
+enum {
+  DEMON_OK = 0,
+  DEMON_ERR_INVALID = 1,     /* bad shape / stride / alignment / null pointer */
+  DEMON_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  DEMON_ERR_TIMEOUT = 3,     /* a device-side bounded wait expired */
+  DEMON_ERR_UNSUPPORTED = 4  /* device is not sm_100 */
+};
+
+/* Global-scale policy of the activation quantiser. */
+enum {
+  DEMON_GS_STATIC = 0,  /* gs[0] supplied by the caller (calibrated) */
+  DEMON_GS_DYNAMIC = 1, /* gs[0] = max(amax(x), 1e-12) / 2688, written (two passes) */
+  DEMON_GS_PER_ROW = 2  /* gs[m] = max(amax(x[m,:]), 1e-12) / 2688, written (one pass,
+                           batch-invariant: a row's codes never depend on other rows) */
+};
+
+DEMON_API int demon_abi_version(void);
+
+/* sizeof(DemonGemmArgs) and sizeof(DemonOdeSlot) as compiled, for binding checks. */
+DEMON_API int demon_struct_sizes(int64_t* gemm_args, int64_t* ode_slot);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated). */
+DEMON_API int demon_last_error(char* buf, size_t n);
+
+/* Reads the device status word of the current device into out[0..1]
+ * (out[0]: DEMON_DEV_* bits, out[1]: first failing site) and clears it.
+ * Synchronises `stream`. */
+DEMON_API int demon_device_status(unsigned int* out_host, void* stream);
+
+/* Bytes of a block-scale buffer for `rows` x K in the tcgen05 layout
+ * (rows padded to 128, K/16 scales per row). */
+DEMON_API int64_t demon_nvfp4_sf_bytes(int64_t rows, int64_t K);
+
+/*
+ * NVFP4 activation quantiser: bf16 x[M, ldx] -> E2M1 codes[M, K/2] (two per
+ * byte, element 2j in the low nibble), E4M3 block scales sf (16-element blocks
+ * along K, tcgen05 128x4-chunk layout, demon_nvfp4_sf_bytes(M, K) bytes, pad
+ * rows written as zero) and fp32 global scale(s) gs.
+ * Stands in for the activation Q node of the reference's quantised linear
+ * (acestep/engine/trt/fp8_onnx.py:847-952, per-tensor FP8 W8A8 activations)
+ * and its weight quantiser (fp8_onnx.py:115-149).  K % 64 == 0, ldx % 8 == 0.
+ */
+DEMON_API int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, float* gs,
+                         uint8_t* codes, uint8_t* sf, void* stream);
+
+/*
+ * Block-scaled NVFP4 GEMM with fused epilogue:
+ *   acc[m,n] = sum_k a[m,k] * w[n,k]                        (tcgen05, fp32 in TMEM)
+ *   y[m,n]   = alpha_m * (acc[m,n] + lora[m,n]) + bias[n]   alpha_m = a_gs[m|0] * w_gs[0]
+ *   lora     = sum_j lora_xa[m,j] * lora_b[n,j]             (tcgen05 bf16 MMA into the same
+ *                                                            accumulator; lora_xa comes from
+ *                                                            demon_lora_down, already divided
+ *                                                            by alpha_m and multiplied by the
+ *                                                            strength)
+ *   y        = gate[m / gate_rows, n] * y                   (optional AdaLN gate)
+ *   out[m,n] = residual[m,n] + y                            (optional), stored as bf16.
+ * Stands in for the DiT nn.Linear call sites (acestep/models/modeling_acestep_v15_turbo.py:
+ * 286-289, 311-345, 377, 538) plus the gated residual that follows o_proj / MLP
+ * (turbo.py:525-546), and for the LoRA writeback W = base + sum s_i B_i A_i
+ * (acestep/engine/lora.py:283-366, 811-833) without rewriting W.
+ * Constraints: K % 256 == 0, N % 32 == 0, ldo/ldr % 8 == 0, lora_rank % 16 == 0 and <= 128.
+ */
+typedef struct DemonGemmArgs {
+  const uint8_t* a_codes; /* [M, K/2] */
+  const uint8_t* a_sf;    /* demon_nvfp4_sf_bytes(M, K) */
+  const float* a_gs;      /* [1] or [M] */
+  int32_t a_gs_per_row;
+  int32_t _pad0;
+  const uint8_t* w_codes; /* [N, K/2] */
+  const uint8_t* w_sf;    /* demon_nvfp4_sf_bytes(N, K) */
+  const float* w_gs;      /* [1] */
+  int64_t M, N, K;
+  void* out;              /* bf16 [M, ldo] */
+  int64_t ldo;
+  const void* bias;       /* bf16 [N] or NULL */
+  const void* residual;   /* bf16 [M, ldr] or NULL (may alias out) */
+  int64_t ldr;
+  const void* gate;       /* bf16 [M / gate_rows, ld_gate] or NULL */
+  int64_t gate_rows;      /* rows per gate row (sequence length) */
+  int64_t ld_gate;
+  const void* lora_xa;    /* bf16 [M, lora_rank] or NULL */
+  const void* lora_b;     /* bf16 [N, lora_rank] */
+  int64_t lora_rank;
+} DemonGemmArgs;
+
+DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);
+
+/*
+ * LoRA down-projection for the fused epilogue (tcgen05 bf16 GEMM):
+ *   xa[m, j] = col_scale[j] * sum_k x[m,k] * lora_a[j,k] / (a_gs[m|0] * w_gs[0])
+ * x bf16 [M, ldx], lora_a bf16 [rank, K] (PEFT lora_A layout, acestep/engine/lora.py:294-302),
+ * col_scale fp32 [rank] (the strength of the LoRA each rank column belongs to),
+ * xa bf16 [M, rank].  K % 64 == 0, rank % 16 == 0, rank <= 128.
+ */
+DEMON_API int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* lora_a, int64_t rank,
+                    const float* col_scale, const float* a_gs, int a_gs_per_row, const float* w_gs, void* xa,
+                    void* stream);
+
+/*
+ * Fused per-slot ODE step over one tick (all slots in one launch).
+ * Stands in for StreamPipeline._tick_pt's post-forward section
+ * (acestep/engine/stream.py:983-998, 1060-1276) composed from
+ * acestep/engine/ode_steps.py:72-392 (x0_from_vel, mask_pre_blend,
+ * mask_post_blend_x0, blend_x0_target, blend_velocities, step_ode_euler,
+ * step_sde_curve, step_sde_renoise, MomentumBuffer, apg_forward, cfg_rescale).
+ * All latents are bf16 [T, D] row-major with D == 64; curves are fp32 [T].
+ * A NULL curve pointer means "use the scalar field next to it".
+ */
+enum {
+  DEMON_ODE_X0PATH = 1 << 0,      /* x0-blend integration (needs_x0 in stream.py:1188-1194) */
+  DEMON_ODE_MASK = 1 << 1,        /* latent mask: pre-blend base, post-blend x0 */
+  DEMON_ODE_CFG = 1 << 2,         /* APG guidance (apg_forward) */
+  DEMON_ODE_MOM_INIT = 1 << 3,    /* momentum running average starts at 0 */
+  DEMON_ODE_RESCALE = 1 << 4,     /* cfg_rescale */
+  DEMON_ODE_X0_TARGET = 1 << 5,   /* x0 = (1-c) x0 + c * x0_target */
+  DEMON_ODE_FINAL = 1 << 6,       /* t_next <= 0 */
+  DEMON_ODE_SDE_CURVE = 1 << 7,   /* step_sde_curve */
+  DEMON_ODE_SDE_BARE = 1 << 8,    /* step_sde_renoise */
+  DEMON_ODE_ONC = 1 << 9,         /* ode_noise_curve injection */
+  DEMON_ODE_CACHE_NEG = 1 << 10,  /* write v_neg into neg_cache (RCFG initialize, step 0) */
+  DEMON_ODE_DEC_OUT = 1 << 11,    /* write next tick's decoder input */
+  DEMON_ODE_DEC_MASK = 1 << 12,   /* next decoder input is mask-pre-blended */
+  DEMON_ODE_VS = 1 << 13          /* velocity_scale present */
+};
+
+#define DEMON_ODE_MAX_COND 4
+
+typedef struct DemonOdeSlot {
+  void* xt;                                    /* in: state x_t; out: x_{t_next} (in place) */
+  const void* v_pos[DEMON_ODE_MAX_COND];       /* positive velocities, one per active condition */
+  const float* w_pos[DEMON_ODE_MAX_COND];      /* temporal weights [T] (NULL = 1) */
+  const void* v_neg[DEMON_ODE_MAX_COND];       /* negative velocities (forward, cache or initial noise) */
+  const float* w_neg[DEMON_ODE_MAX_COND];
+  int32_t n_pos, n_neg;
+  void* neg_cache;                             /* RCFG initialize cache (written with CACHE_NEG) */
+  void* momentum;                              /* APG running average [T, D] (in/out) */
+  const float* guidance; float guidance_s;     /* APG guidance scale */
+  const float* apg_mom; float apg_mom_s;       /* APG momentum */
+  const float* rescale; float rescale_s;       /* cfg_rescale blend */
+  const float* vscale; float vscale_s;         /* velocity_scale */
+  const float* sdc; float sdc_s;               /* sde_denoise_curve */
+  const float* onc; float onc_s;               /* ode_noise_curve */
+  const float* x0_coef; float x0_coef_s;       /* x0_target blend coefficient (times x0_coef_mul) */
+  float x0_coef_mul;
+  float mask_s;                                /* mask strength at this step */
+  const float* mask;                           /* [T] latent mask (1 = generate) */
+  const void* mask_orig;                       /* [T, D] original latents */
+  const void* mask_noise;                      /* [T, D] fixed mask noise */
+  const void* source;                          /* [T, D] source latents (SDE curve) */
+  const void* x0_target;                       /* [T, D] */
+  const void* noise;                           /* [T, D] step noise (NULL = in-kernel Philox) */
+  void* dec_out;                               /* [T, D] next decoder input */
+  float mask_s_next;                           /* mask strength at the next step */
+  float t_curr, t_next;
+  int32_t flags;
+  uint64_t seed;                               /* Philox key for in-kernel noise */
+  uint64_t step;                               /* Philox counter offset (step index) */
+} DemonOdeSlot;
+
+/*
+ * slots: device array of n_slots DemonOdeSlot (the library reads it on the device);
+ * gain: bf16 [T, D] channel gain applied to the next decoder input (NULL = 1);
+ * T: frames per slot (all slots share T, as StreamPipeline.tick enforces,
+ * stream.py:867-883); D must be 64.
+ */
+DEMON_API int demon_ode_step(const DemonOdeSlot* slots_dev, int32_t n_slots, int64_t T, int64_t D, const void* gain,
+                   void* stream);
+
+/*
+ * Decoder-input preparation for newly initialised slots (stream.py:983-998):
+ * dec_out = (mask ? mask_pre_blend(xt) : xt) * gain, per slot, using
+ * t_curr / mask_s / DEMON_ODE_MASK of each slot descriptor.
+ */
+DEMON_API int demon_ode_prepare(const DemonOdeSlot* slots_dev, int32_t n_slots, int64_t T, int64_t D, const void* gain,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DEMON_B200_H */
