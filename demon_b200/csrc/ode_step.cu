@@ -123,13 +123,24 @@ __device__ __forceinline__ void blend(const void* const* v, const float* const* 
   for (int j = 0; j < 4; ++j) out[j] = rnd(num[j] * inv);
 }
 
-// mask_pre_blend (ode_steps.py:89-106): m x + (1 - m)(t noise + (1 - t) orig)
+// mask_pre_blend (ode_steps.py:89-106): m x + (1 - m)(t noise + (1 - t) orig),
+// rounded after every operation as the reference's eager bf16 tensors are
+// (the products and sums of bf16 operands are exact in fp32, so this is bit-exact).
 __device__ __forceinline__ void pre_blend(const DemonOdeSlot& S, int64_t off, float m, float t, float (&x)[4]) {
   float o[4], nz[4];
   ld4(S.mask_orig, off, o);
   ld4(S.mask_noise, off, nz);
+  const float om = rnd(1.0f - m), ot = 1.0f - t;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = rnd(m * x[j] + (1.0f - m) * (t * nz[j] + (1.0f - t) * o[j]));
+  for (int j = 0; j < 4; ++j) {
+    const float noised = rnd(rnd(t * nz[j]) + rnd(ot * o[j]));
+    x[j] = rnd(rnd(m * x[j]) + rnd(om * noised));
+  }
+}
+
+// (1 - c) x + c y, op by op (mask_post_blend_x0 / blend_x0_target, ode_steps.py:109-142)
+__device__ __forceinline__ float lerp_eager(float x, float c, float y) {
+  return rnd(rnd(rnd(1.0f - c) * x) + rnd(c * y));
 }
 
 __device__ __forceinline__ void write_dec(const DemonOdeSlot& S, const __nv_bfloat16* gain, int64_t off, int t,
@@ -169,7 +180,7 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
       const int64_t off = (int64_t)t * kOdeD + c0;
       float x[4];
       ld4(S.xt, off, x);
-      const float m = (flags & DEMON_ODE_DEC_MASK) ? __ldg(S.mask + t) * S.mask_s : 0.f;
+      const float m = (flags & DEMON_ODE_DEC_MASK) ? rnd(__ldg(S.mask + t) * S.mask_s) : 0.f;
       write_dec(S, gain, off, t, (flags & DEMON_ODE_DEC_MASK) != 0, m, S.t_curr, x);
     }
     return;
@@ -295,7 +306,7 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
       }
     }
     ld4(S.xt, off, x);
-    const float m = mask ? __ldg(S.mask + t) * S.mask_s : 1.f;
+    const float m = mask ? rnd(__ldg(S.mask + t) * S.mask_s) : 1.f;
     if (mask) pre_blend(S, off, m, tc, x);
     const float vs = (flags & DEMON_ODE_VS) ? rnd(curve(S.vscale, S.vscale_s, t)) : 1.f;
     const float onc = onc_on ? rnd(curve(S.onc, S.onc_s, t)) : 0.f;
@@ -311,19 +322,20 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
     } else {
       float x0[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x0[j] = rnd(x[j] - rnd(vt[j] * vs) * tc);
+      for (int j = 0; j < 4; ++j) x0[j] = rnd(x[j] - rnd(rnd(vt[j] * vs) * tc));
       if (mask) {
         float o[4];
         ld4(S.mask_orig, off, o);
+        const float om = rnd(1.0f - m);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x0[j] = rnd(m * x0[j] + (1.0f - m) * o[j]);
+        for (int j = 0; j < 4; ++j) x0[j] = rnd(rnd(m * x0[j]) + rnd(om * o[j]));
       }
       if (flags & DEMON_ODE_X0_TARGET) {
         float tg[4];
         ld4(S.x0_target, off, tg);
         const float c = rnd(curve(S.x0_coef, S.x0_coef_s, t) * S.x0_coef_mul);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x0[j] = rnd((1.0f - c) * x0[j] + c * tg[j]);
+        for (int j = 0; j < 4; ++j) x0[j] = lerp_eager(x0[j], c, tg[j]);
       }
       if (sde_curve) {
         float src[4];
@@ -346,7 +358,7 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float vb = rnd(__fdiv_rn(x[j] - x0[j], tc));
+          const float vb = rnd(__fdiv_rn(rnd(x[j] - x0[j]), tc));
           xn[j] = x[j] + dt * vb + eps[j] * onc * tn;
         }
       }
@@ -356,7 +368,7 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
     st4(S.xt, off, xn);
     if (flags & DEMON_ODE_DEC_OUT) {
       const bool dm = (flags & DEMON_ODE_DEC_MASK) != 0;
-      const float mn = dm ? __ldg(S.mask + t) * S.mask_s_next : 0.f;
+      const float mn = dm ? rnd(__ldg(S.mask + t) * S.mask_s_next) : 0.f;
       write_dec(S, gain, off, t, dm, mn, tn, xn);
     }
   }
