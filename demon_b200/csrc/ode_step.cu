@@ -118,9 +118,9 @@ __device__ __forceinline__ void blend(const void* const* v, const float* const* 
     for (int j = 0; j < 4; ++j) num[j] = fmaf(x[j], wi, num[j]);
     den += wi;
   }
-  const float inv = 1.0f / fmaxf(den, 1e-8f);
+  const float dd = fmaxf(den, 1e-8f);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) out[j] = rnd(num[j] * inv);
+  for (int j = 0; j < 4; ++j) out[j] = rnd(__fdiv_rn(num[j], dd));
 }
 
 // mask_pre_blend (ode_steps.py:89-106): m x + (1 - m)(t noise + (1 - t) orig),

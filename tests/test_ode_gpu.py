@@ -166,7 +166,9 @@ def test_ode_step_matches_oracle(cuda, T):
         scale = np.maximum(np.abs(ref["xt"]), np.abs(s["xt"]))
         check(f"{k}:xt", st.xt, ref["xt"], scale)
         if "momentum" in ref:
-            check(f"{k}:momentum", st.momentum, ref["momentum"], np.abs(ref["momentum"]))
+            # v_pos - v_neg can cancel: measure in ulps of the velocities' magnitude
+            vmag = np.maximum(np.abs(s["pos"][0][0]), np.abs(ref["momentum"]))
+            check(f"{k}:momentum", st.momentum, ref["momentum"], vmag)
         if "neg_cache" in ref:
             assert np.array_equal(st.neg_cache_out.float().cpu().numpy(), ref["neg_cache"]), k
         if "dec" in ref:
