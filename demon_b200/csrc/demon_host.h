@@ -21,9 +21,10 @@ bool device_pending(const std::atomic<uint64_t>& flags);
 void mark_device_done(std::atomic<uint64_t>& flags);
 
 // 2-D row-major tiled tensor map: `rows` x `cols` elements of `elem_bytes`,
-// row pitch `ld_bytes`, box `box_rows` x `box_cols`, 128-byte swizzle.
+// row pitch `ld_bytes`, box `box_rows` x `box_cols`, given swizzle (default 128-byte).
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
-                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows);
+                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 }  // namespace demon
 

@@ -1,23 +1,33 @@
 // nvfp4_gemm.cu -- tcgen05 block-scaled NVFP4 GEMM with fused epilogue (sm_100a),
 // and the bf16 tcgen05 GEMM used for the LoRA down-projection.
 //
-// One CTA computes a 128 x BN output tile.  Warp roles (192 threads):
+// Persistent kernel: one CTA per SM walks output tiles of 128 x BN
+// (tile t = blockIdx.x + i * gridDim.x, M fastest so concurrent CTAs share the
+// B tiles in L2).  Warp roles (320 threads):
 //   warp 0      TMA producer: A/B tiles with tiled TMA loads (128-byte swizzle,
-//               no multicast) and the block scales of the stage with untiled
-//               bulk copies -- the quantiser writes scales directly in the
-//               tcgen05 128x4-chunk layout, so a stage's scales are contiguous.
-//   warp 1      TMEM allocation + a single MMA-issuing thread: per stage it
-//               copies the scales SMEM -> TMEM (tcgen05.cp 32x128b.warpx4,
-//               replicated into the four lane quadrants), then issues four
-//               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each),
+//               no multicast) and the stage's block scales with untiled bulk
+//               copies -- the quantiser writes scales in the tcgen05 128x4-chunk
+//               layout, so a stage's scales are contiguous.  It runs ahead into
+//               the next tile while the epilogue drains the current one.
+//   warp 1      TMEM allocation + one MMA-issuing thread: per stage it copies
+//               the scales SMEM -> TMEM (tcgen05.cp 32x128b.warpx4, replicated
+//               into the four lane quadrants), issues four
+//               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
 //               and commits to the stage's "empty" barrier.
-//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one row per
-//               thread), alpha * acc + bias, optional gate * y and residual +,
-//               bf16 stores.
-// Hot LoRA: the rank-r product xa . B^T is one extra group of kind::f16 MMAs
-// into the same TMEM accumulator before the FP4 K-loop; xa is pre-divided by
-// alpha and pre-multiplied by the strength (demon_lora_down), so changing the
-// strength never touches the packed weights.
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant, each owning half of
+//               the tile's columns.  They drain their accumulator columns into
+//               registers with tcgen05.ld and release TMEM right away (the MMA
+//               warp starts the next tile while the epilogue computes
+//               alpha * acc + bias, gate * y, residual + y and stores), then
+//               stage 32x32 bf16 blocks in swizzled shared memory and write
+//               them with TMA stores.  A residual block is TMA-loaded into the
+//               same staging buffer and updated in place.
+// Hot LoRA: for each 64-wide slice of the rank, one extra pipeline stage holds
+// the xa tile (128 x 64 bf16, 16 KB -- the size of an A stage) and the
+// lora_b tile (BN x 64 bf16 -- the size of a B stage); four kind::f16 MMAs
+// accumulate xa . lora_b^T into the same TMEM accumulator before the FP4
+// K-loop.  xa is pre-divided by alpha and pre-multiplied by the strength
+// (demon_lora_down), so a strength change never touches the packed weights.
 //
 // Every mbarrier wait is bounded (demon_common.cuh); on expiry the CTA records
 // DEMON_DEV_TIMEOUT, stops issuing, drains what it issued and frees TMEM.
@@ -37,48 +47,48 @@ struct GemmParams {
   const float* a_gs;
   const float* w_gs;
   const float* col_scale;  // bf16 mode: per-output-column scale
-  __nv_bfloat16* out;
   const __nv_bfloat16* bias;
-  const __nv_bfloat16* residual;
   const __nv_bfloat16* gate;
   unsigned int* status;
-  int64_t ldo, ldr, gate_rows, ld_gate;
+  int64_t gate_rows, ld_gate;
   int M, N, K;
   int a_gs_per_row;
   int lora_rank;
+  int has_residual;
+  int m_tiles, n_tiles;
 };
 
 constexpr int kBM = 128;
-constexpr int kRowBytes = 128;  // one 128-byte swizzle row per stage (256 fp4 / 64 bf16)
+constexpr int kRowBytes = 128;   // one 128-byte swizzle row per stage (256 fp4 / 64 bf16)
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageBuf = 2048;  // 32 rows x 32 bf16, 64-byte swizzle
 
-template <int BN, int STAGES, bool FP4, int LBOX>
+template <int BN, int STAGES, bool FP4>
 struct GemmCfg {
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = BN * kRowBytes;
   static constexpr int kSFA = FP4 ? 2048 : 0;
-  static constexpr int kSFB = FP4 ? (BN / 128) * 2048 : 0;
-  static constexpr int kLoraBoxes = LBOX;  // LoRA boxes of 64 bf16 along the rank
-  static constexpr int kLA = kBM * kRowBytes;
-  static constexpr int kLB = BN * kRowBytes;
+  static constexpr int kSFB = FP4 ? ((BN + 127) / 128) * 2048 : 0;
   static constexpr int offA = 0;
   static constexpr int offB = offA + STAGES * kA;
-  static constexpr int offLA = offB + STAGES * kB;
-  static constexpr int offLB = offLA + kLoraBoxes * kLA;
-  static constexpr int offSFA = offLB + kLoraBoxes * kLB;
+  static constexpr int offSFA = offB + STAGES * kB;
   static constexpr int offSFB = offSFA + STAGES * kSFA;
-  static constexpr int offBar = offSFB + STAGES * kSFB;
-  static constexpr int kBars = 2 * STAGES + 2;
+  static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
+  static constexpr int offBar = offStg + kEpiWarps * 2 * kStageBuf;
+  static constexpr int kBars = 2 * STAGES + 3 + 2 * kEpiWarps;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
-  static constexpr int kAccCols = BN;
-  static constexpr int kSfaCol = BN;            // 4 columns per K=64 step, 4 steps
-  static constexpr int kSfbCol = BN + 16;       // BN/32 columns per step, 4 steps
-  static constexpr int kUsedCols = FP4 ? BN + 16 + (BN / 32) * 4 : BN;
+  static constexpr int kSfaCol = BN;                 // 4 columns per K=64 step, 4 steps
+  static constexpr int kSfbCol = BN + 16;            // ((BN+127)/128)*4 columns per step
+  static constexpr int kUsedCols = FP4 ? BN + 16 + ((BN + 127) / 128) * 16 : BN;
   static constexpr uint32_t kTmemCols = kUsedCols <= 32 ? 32 : kUsedCols <= 64 ? 64 : kUsedCols <= 128 ? 128
                                         : kUsedCols <= 256 ? 256 : 512;
   static constexpr int kStepElems = FP4 ? 256 : 64;  // K elements per stage
+  static constexpr int kColsPerWarp = BN / 2;        // columns per epilogue warp
+  static constexpr int kChunks = kColsPerWarp / 32;  // 32-column chunks per epilogue warp
   static_assert(kSmem <= 232448, "shared memory budget");
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
@@ -89,27 +99,32 @@ __device__ __forceinline__ uint64_t sf_desc(const void* p) {
   // 32 rows x 16 bytes, no swizzle: 8-row core matrices 128 bytes apart.
   return smem_desc(smem_u32(p), 0, 128, 0);
 }
+// Byte offset of 16-byte chunk j of row r in a 32 x 64-byte staging block with
+// the TMA 64-byte swizzle (address bits [4,5] ^= bits [7,8]).
+__device__ __forceinline__ int stg_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
-template <int BN, int STAGES, bool FP4, int LBOX>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int STAGES, bool FP4>
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
+                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                 const GemmParams p) {
-  using C = GemmCfg<BN, STAGES, FP4, LBOX>;
-  constexpr bool LORA = LBOX > 0;
+  using C = GemmCfg<BN, STAGES, FP4>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::offBar);
   uint64_t* empty = full + STAGES;
-  uint64_t* lora_full = empty + STAGES;
-  uint64_t* acc_full = lora_full + 1;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint64_t* res_full = mma_done + 1;  // [kEpiWarps][2]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::offMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::offMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_blk = blockIdx.x, m_blk = blockIdx.y;
-  const int m0 = m_blk * kBM, n0 = n_blk * BN;
   const int KT = p.K / C::kStepElems;
+  const int lboxes = p.lora_rank > 0 ? (p.lora_rank + 63) / 64 : 0;
+  const int num_tiles = p.m_tiles * p.n_tiles;
   const uint64_t t0 = globaltimer();
 
   if (threadIdx.x == 0) {
@@ -117,18 +132,22 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(lora_full, 1);
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kEpiWarps);
+    mbar_init(mma_done, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if (LORA) {
+    prefetch_tmap(&tmOut);
+    if (lboxes) {
       prefetch_tmap(&tmLA);
       prefetch_tmap(&tmLB);
     }
+    if (p.has_residual) prefetch_tmap(&tmRes);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::kTmemCols);
@@ -142,44 +161,43 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
-      int issued = 0;
-      const int lboxes = LORA ? (p.lora_rank + 63) / 64 : 0;
-      if (LORA) {
-        mbar_arrive_expect_tx(lora_full, (uint32_t)lboxes * (C::kLA + C::kLB));
-        for (int b = 0; b < lboxes; ++b) {
-          tma_load_2d(smem + C::offLA + b * C::kLA, &tmLA, lora_full, b * 64, m0);
-          tma_load_2d(smem + C::offLB + b * C::kLB, &tmLB, lora_full, b * 64, n0);
-        }
-      }
-      // scale halves of the B tile that exist in the (128-row padded) scale buffer
-      const int sfb_halves = FP4 ? std::min(BN / 128, (p.N - n0 + 127) / 128) : 0;
-      const uint32_t tx = (uint32_t)(C::kA + C::kB + C::kSFA + sfb_halves * 2048);
+      uint32_t g = 0;  // stages issued so far (all tiles)
       const int64_t kchunks = p.K / 64;
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, t0, p.status, 1)) break;
-        mbar_arrive_expect_tx(&full[s], tx);
-        const int kx = FP4 ? kt * kRowBytes : kt * 64;
-        tma_load_2d(smem + C::offA + s * C::kA, &tmA, &full[s], kx, m0);
-        tma_load_2d(smem + C::offB + s * C::kB, &tmB, &full[s], kx, n0);
-        if (FP4) {
-          bulk_load(smem + C::offSFA + s * C::kSFA, p.a_sf + ((int64_t)m_blk * kchunks + kt * 4) * 512, 2048,
-                    &full[s]);
-          for (int h = 0; h < sfb_halves; ++h)
-            bulk_load(smem + C::offSFB + s * C::kSFB + h * 2048,
-                      p.w_sf + ((int64_t)(n_blk * (BN / 128) + h) * kchunks + kt * 4) * 512, 2048, &full[s]);
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+        const int m0 = m_blk * kBM, n0 = n_blk * BN;
+        for (int b = 0; b < lboxes; ++b, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 1))) break;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::kA + C::kB));
+          tma_load_2d(smem + C::offA + s * C::kA, &tmLA, &full[s], b * 64, m0);
+          tma_load_2d(smem + C::offB + s * C::kB, &tmLB, &full[s], b * 64, n0);
         }
-        ++issued;
+        // scale halves of the B tile that exist in the (128-row padded) scale buffer
+        const int sfb_halves = FP4 ? std::min((BN + 127) / 128, (p.N - n0 + 127) / 128) : 0;
+        const uint32_t tx = (uint32_t)(C::kA + C::kB + C::kSFA + sfb_halves * 2048);
+        for (int kt = 0; ok && kt < KT; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 2))) break;
+          mbar_arrive_expect_tx(&full[s], tx);
+          const int kx = FP4 ? kt * kRowBytes : kt * 64;
+          tma_load_2d(smem + C::offA + s * C::kA, &tmA, &full[s], kx, m0);
+          tma_load_2d(smem + C::offB + s * C::kB, &tmB, &full[s], kx, n0);
+          if (FP4) {
+            bulk_load(smem + C::offSFA + s * C::kSFA, p.a_sf + ((int64_t)m_blk * kchunks + kt * 4) * 512, 2048,
+                      &full[s]);
+            for (int h = 0; h < sfb_halves; ++h)
+              bulk_load(smem + C::offSFB + s * C::kSFB + h * 2048,
+                        p.w_sf + ((int64_t)(n_blk * ((BN + 127) / 128) + h) * kchunks + kt * 4) * 512, 2048,
+                        &full[s]);
+          }
+        }
       }
-      // drain: never leave the CTA with copies in flight (no-op on the normal path)
-      for (int i = std::max(0, issued - STAGES); i < issued; ++i) {
+      // drain: never leave the CTA with copies in flight (returns at once on the normal path)
+      for (uint32_t i = g > (uint32_t)STAGES ? g - STAGES : 0; i < g; ++i) {
         volatile int never = 0;
-        mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, &never, globaltimer(), p.status, 2);
-      }
-      if (LORA) {
-        volatile int never = 0;
-        mbar_wait(lora_full, 0, &never, globaltimer(), p.status, 3);
+        mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never, globaltimer(), p.status, 3);
       }
     }
     __syncwarp();
@@ -187,128 +205,176 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       const uint32_t idesc = FP4 ? idesc_mxf4nvf4(kBM, BN) : idesc_bf16(kBM, BN);
-      const uint32_t d_acc = tmem;
-      uint32_t accum = 0;
+      const uint32_t ib = idesc_bf16(kBM, BN);
+      uint32_t g = 0, it = 0;
       bool ok = true;
-      if (LORA) {
-        ok = mbar_wait(lora_full, 0, abort_flag, t0, p.status, 4);
-        if (ok) {
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
+        // the epilogue must have drained the previous tile's accumulator
+        if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4))) break;
+        tc_fence_after();
+        uint32_t accum = 0;
+        for (int b = 0; b < lboxes; ++b, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 5))) break;
           tc_fence_after();
-          const uint32_t ib = idesc_bf16(kBM, BN);
-          for (int b = 0; b < LBOX; ++b) {
-            const uint64_t la = sw128_desc(smem + C::offLA + b * C::kLA);
-            const uint64_t lb = sw128_desc(smem + C::offLB + b * C::kLB);
-            for (int j = 0; j < 4; ++j) {
-              if (b * 64 + j * 16 < p.lora_rank) {
-                mma_bf16(d_acc, la + 2 * j, lb + 2 * j, ib, accum);
-                accum = 1;
-              }
+          const uint64_t la = sw128_desc(smem + C::offA + s * C::kA);
+          const uint64_t lb = sw128_desc(smem + C::offB + s * C::kB);
+          for (int j = 0; j < 4; ++j) {
+            if (b * 64 + j * 16 < p.lora_rank) {
+              mma_bf16(tmem, la + 2 * j, lb + 2 * j, ib, accum);
+              accum = 1;
             }
           }
+          tc_commit(&empty[s]);
         }
-      }
-      for (int kt = 0; ok && kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, abort_flag, t0, p.status, 5)) break;
-        tc_fence_after();
-        const uint64_t adesc = sw128_desc(smem + C::offA + s * C::kA);
-        const uint64_t bdesc = sw128_desc(smem + C::offB + s * C::kB);
-        if (FP4) {
-          const uint8_t* sfa = smem + C::offSFA + s * C::kSFA;
-          const uint8_t* sfb = smem + C::offSFB + s * C::kSFB;
+        for (int kt = 0; ok && kt < KT; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 6))) break;
+          tc_fence_after();
+          const uint64_t adesc = sw128_desc(smem + C::offA + s * C::kA);
+          const uint64_t bdesc = sw128_desc(smem + C::offB + s * C::kB);
+          if (FP4) {
+            const uint8_t* sfa = smem + C::offSFA + s * C::kSFA;
+            const uint8_t* sfb = smem + C::offSFB + s * C::kSFB;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tc_cp_32x128b_warpx4(tmem + C::kSfaCol + 4 * j, sf_desc(sfa + j * 512));
+            for (int j = 0; j < 4; ++j) {
+              tc_cp_32x128b_warpx4(tmem + C::kSfaCol + 4 * j, sf_desc(sfa + j * 512));
 #pragma unroll
-            for (int h = 0; h < BN / 128; ++h)
-              tc_cp_32x128b_warpx4(tmem + C::kSfbCol + (BN / 32) * j + 4 * h, sf_desc(sfb + h * 2048 + j * 512));
+              for (int h = 0; h < (BN + 127) / 128; ++h)
+                tc_cp_32x128b_warpx4(tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j + 4 * h,
+                                     sf_desc(sfb + h * 2048 + j * 512));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_mxf4nvf4(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + C::kSfaCol + 4 * j,
+                           tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j, accum);
+              accum = 1;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_bf16(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, accum);
+              accum = 1;
+            }
           }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            mma_mxf4nvf4(d_acc, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + C::kSfaCol + 4 * j,
-                         tmem + C::kSfbCol + (BN / 32) * j, accum);
-            accum = 1;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            mma_bf16(d_acc, adesc + 2 * j, bdesc + 2 * j, idesc, accum);
-            accum = 1;
-          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        tc_commit(acc_full);
       }
-      tc_commit(acc_full);
-      // wait for our own MMAs before anyone frees TMEM (returns at once normally)
+      if (!ok) tc_commit(acc_full);  // wake the epilogue on the abort path
+      // every MMA of this CTA has completed before anyone frees TMEM
+      tc_commit(mma_done);
       volatile int never = 0;
-      mbar_wait(acc_full, 0, &never, globaltimer(), p.status, 6);
+      mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant accessible to this warp
-    const int64_t row = (int64_t)m0 + q * 32 + lane;
-    const bool ok = mbar_wait(acc_full, 0, abort_flag, t0, p.status, 7);
-    tc_fence_after();
-    if (ok && !*abort_flag) {
+    const int ew = warp - 2;            // 0..7
+    const int q = warp & 3;             // TMEM lane quadrant accessible to this warp
+    const int half = ew >> 2;           // which half of the tile's columns
+    uint8_t* stg = smem + C::offStg + ew * 2 * kStageBuf;
+    uint64_t* rbar = res_full + ew * 2;
+    uint32_t it = 0, nchunk = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      const int m0 = m_blk * kBM, n0 = n_blk * BN;
+      if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7)) break;
+      tc_fence_after();
+      if (*abort_flag) break;
+      uint32_t v[C::kChunks][32];
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c)
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * C::kColsPerWarp + c * 32), v[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);  // TMEM drained: the next tile's MMAs may start
+
+      const int r_loc = q * 32 + lane;
+      const int64_t row = (int64_t)m0 + r_loc;
       const bool row_ok = row < p.M;
       const float ga = row_ok ? p.a_gs[p.a_gs_per_row ? row : 0] : 0.0f;
       const float alpha = ga * p.w_gs[0];
+      const float inv_alpha = FP4 ? 0.0f : (row_ok ? 1.0f / alpha : 0.0f);
       const __nv_bfloat16* gate_row = (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < (BN + 31) / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
-        tmem_ld_wait();
-        const int n = n0 + c * 32;
-        if (!row_ok) continue;
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          const int nn = n + g8 * 8;
-          if (nn >= p.N || c * 32 + g8 * 8 >= BN) break;
-          float y[8];
-          if (FP4) {
+      for (int c = 0; c < C::kChunks; ++c, ++nchunk) {
+        const int ncol = n0 + half * C::kColsPerWarp + c * 32;
+        if (ncol >= p.N) break;  // uniform across the warp
+        uint8_t* buf = stg + (nchunk & 1) * kStageBuf;
+        uint64_t* rb = rbar + (nchunk & 1);
+        // the TMA store that last read this buffer (two chunks ago) must be done reading
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        if (FP4 && p.has_residual) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(rb, kStageBuf);
+            tma_load_2d(buf, &tmRes, rb, ncol, m0 + q * 32);
+          }
+          mbar_wait(rb, (nchunk >> 1) & 1u, abort_flag, t0, p.status, 8);
+        }
+        float y[32];
+        if (FP4) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
             uint4 bb = make_uint4(0u, 0u, 0u, 0u);
-            if (p.bias) bb = *reinterpret_cast<const uint4*>(p.bias + nn);
+            if (p.bias) bb = __ldg(reinterpret_cast<const uint4*>(p.bias + ncol) + j);
             const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              y[2 * i] = fmaf(alpha, __uint_as_float(v[g8 * 8 + 2 * i]), bf16_lo(bw[i]));
-              y[2 * i + 1] = fmaf(alpha, __uint_as_float(v[g8 * 8 + 2 * i + 1]), bf16_hi(bw[i]));
+              y[8 * j + 2 * i] = fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i]), bf16_lo(bw[i]));
+              y[8 * j + 2 * i + 1] = fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i + 1]), bf16_hi(bw[i]));
             }
-            if (gate_row) {
-              const uint4 gg = *reinterpret_cast<const uint4*>(gate_row + nn);
+          }
+          if (gate_row) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 gg = *reinterpret_cast<const uint4*>(gate_row + ncol + 8 * j);
               const uint32_t gw[4] = {gg.x, gg.y, gg.z, gg.w};
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
-                y[2 * i] *= bf16_lo(gw[i]);
-                y[2 * i + 1] *= bf16_hi(gw[i]);
+                y[8 * j + 2 * i] *= bf16_lo(gw[i]);
+                y[8 * j + 2 * i + 1] *= bf16_hi(gw[i]);
               }
             }
-            if (p.residual) {
-              const uint4 rr = *reinterpret_cast<const uint4*>(p.residual + row * p.ldr + nn);
+          }
+          if (p.has_residual) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 rr = *reinterpret_cast<const uint4*>(buf + stg_off(lane, j));
               const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
-                y[2 * i] += bf16_lo(rw[i]);
-                y[2 * i + 1] += bf16_hi(rw[i]);
+                y[8 * j + 2 * i] += bf16_lo(rw[i]);
+                y[8 * j + 2 * i + 1] += bf16_hi(rw[i]);
               }
             }
-          } else {
-            const float inv_alpha = 1.0f / alpha;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[g8 * 8 + i]) * (p.col_scale[nn + i] * inv_alpha);
           }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            y[i] = (ncol + i < p.N) ? __uint_as_float(v[c][i]) * (p.col_scale[ncol + i] * inv_alpha) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
           uint4 o;
-          o.x = pack_bf16x2(y[0], y[1]);
-          o.y = pack_bf16x2(y[2], y[3]);
-          o.z = pack_bf16x2(y[4], y[5]);
-          o.w = pack_bf16x2(y[6], y[7]);
-          *reinterpret_cast<uint4*>(p.out + row * p.ldo + nn) = o;
+          o.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
+          o.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
+          o.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
+          o.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+          *reinterpret_cast<uint4*>(buf + stg_off(lane, j)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmOut, buf, ncol, m0 + q * 32);
+          bulk_commit();
         }
       }
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -319,18 +385,24 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int BN, int STAGES, bool FP4, int LBOX>
+template <int BN, int STAGES, bool FP4>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                const GemmParams& p, cudaStream_t st) {
-  using C = GemmCfg<BN, STAGES, FP4, LBOX>;
-  auto kern = gemm_kernel<BN, STAGES, FP4, LBOX>;
+                const CUtensorMap& out, const CUtensorMap& res, GemmParams p, cudaStream_t st) {
+  using C = GemmCfg<BN, STAGES, FP4>;
+  auto kern = gemm_kernel<BN, STAGES, FP4>;
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {
     DEMON_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     mark_device_done(attr_done);
   }
-  const dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + kBM - 1) / kBM));
-  kern<<<grid, 192, C::kSmem, st>>>(a, b, la, lb, p);
+  int dev = 0, sms = 148;
+  DEMON_CUDA(cudaGetDevice(&dev));
+  DEMON_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  p.m_tiles = (p.M + kBM - 1) / kBM;
+  p.n_tiles = (p.N + BN - 1) / BN;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const dim3 grid((unsigned)std::min(tiles, sms));
+  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, out, res, p);
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
 }
@@ -371,17 +443,22 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                   "gemm: LoRA needs lora_b and rank %% 16 == 0, 0 < rank <= 128 (rank=%lld)",
                   (long long)a->lora_rank);
   if (M == 0) return DEMON_OK;
-  unsigned int* status = status_word();
 
-  const bool bn256 = (N % 256 == 0) && !(lora && a->lora_rank > 64);
+  const bool bn256 = (N % 256 == 0);
   const uint32_t BN = bn256 ? 256 : 128;
-  CUtensorMap ta, tb, tla, tlb;
+  CUtensorMap ta, tb, tla, tlb, tout, tres;
   memset(&tla, 0, sizeof tla);
   memset(&tlb, 0, sizeof tlb);
+  memset(&tres, 0, sizeof tres);
   DEMON_RC(make_tmap_2d(&ta, a->a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)M,
                         (uint64_t)K / 2, 128, 128));
   DEMON_RC(make_tmap_2d(&tb, a->w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)N,
                         (uint64_t)K / 2, 128, BN));
+  DEMON_RC(make_tmap_2d(&tout, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                        (uint64_t)a->ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
+  if (a->residual)
+    DEMON_RC(make_tmap_2d(&tres, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                          (uint64_t)a->ldr * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   if (lora) {
     const uint64_t r = (uint64_t)a->lora_rank;
     DEMON_RC(make_tmap_2d(&tla, a->lora_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)M, r * 2, 64, 128));
@@ -392,13 +469,9 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.w_sf = a->w_sf;
   p.a_gs = a->a_gs;
   p.w_gs = a->w_gs;
-  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
   p.bias = reinterpret_cast<const __nv_bfloat16*>(a->bias);
-  p.residual = reinterpret_cast<const __nv_bfloat16*>(a->residual);
   p.gate = reinterpret_cast<const __nv_bfloat16*>(a->gate);
-  p.status = status;
-  p.ldo = a->ldo;
-  p.ldr = a->ldr;
+  p.status = status_word();
   p.gate_rows = a->gate_rows > 0 ? a->gate_rows : 1;
   p.ld_gate = a->ld_gate;
   p.M = (int)M;
@@ -406,13 +479,10 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.K = (int)K;
   p.a_gs_per_row = a->a_gs_per_row;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
+  p.has_residual = a->residual != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (lora) {
-    if (bn256) return launch_gemm<256, 3, true, 1>(ta, tb, tla, tlb, p, st);
-    return launch_gemm<128, 3, true, 2>(ta, tb, tla, tlb, p, st);
-  }
-  if (bn256) return launch_gemm<256, 4, true, 0>(ta, tb, tla, tlb, p, st);
-  return launch_gemm<128, 4, true, 0>(ta, tb, tla, tlb, p, st);
+  if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, tout, tres, p, st);
+  return launch_gemm<128, 5, true>(ta, tb, tla, tlb, tout, tres, p, st);
 }
 
 extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* lora_a, int64_t rank,
@@ -426,17 +496,17 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   DEMON_CHECK_ARG(x && lora_a && col_scale && a_gs && w_gs && xa, "lora_down: null pointer");
   DEMON_CHECK_ARG(((uintptr_t)xa & 15) == 0, "lora_down: xa must be 16-byte aligned");
   if (M == 0) return DEMON_OK;
-  CUtensorMap ta, tb, tz;
+  CUtensorMap ta, tb, tz, tout;
   memset(&tz, 0, sizeof tz);
   DEMON_RC(make_tmap_2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64,
                         128));
+  DEMON_RC(make_tmap_2d(&tout, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)rank, (uint64_t)M,
+                        (uint64_t)rank * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   GemmParams p{};
   p.a_gs = a_gs;
   p.w_gs = w_gs;
   p.col_scale = col_scale;
-  p.out = reinterpret_cast<__nv_bfloat16*>(xa);
   p.status = status_word();
-  p.ldo = rank;
   p.M = (int)M;
   p.N = (int)rank;
   p.K = (int)K;
@@ -445,9 +515,9 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   if (rank <= 64) {
     DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                           (uint64_t)K * 2, 64, 64));
-    return launch_gemm<64, 6, false, 0>(ta, tb, tz, tz, p, st);
+    return launch_gemm<64, 6, false>(ta, tb, tz, tz, tout, tz, p, st);
   }
   DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                         (uint64_t)K * 2, 64, 128));
-  return launch_gemm<128, 6, false, 0>(ta, tb, tz, tz, p, st);
+  return launch_gemm<128, 6, false>(ta, tb, tz, tz, tout, tz, p, st);
 }

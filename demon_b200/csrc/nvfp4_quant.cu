@@ -18,26 +18,13 @@
 // store (a warp writes 128 contiguous bytes); four block scales that are
 // contiguous in the scale layout are gathered by shuffles into one 32-bit store.
 #include <algorithm>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "demon_common.cuh"
 #include "demon_host.h"
 
 namespace demon {
-
-__device__ __forceinline__ uint32_t e2m1_code(float v) {
-  const float a = fabsf(v);
-  uint32_t mag;
-  if (!(a > 0.25f)) mag = 0;
-  else if (a < 0.75f) mag = 1;
-  else if (a <= 1.25f) mag = 2;
-  else if (a < 1.75f) mag = 3;
-  else if (a <= 2.5f) mag = 4;
-  else if (a < 3.5f) mag = 5;
-  else if (a <= 5.0f) mag = 6;
-  else mag = 7;
-  return (mag != 0u && v < 0.0f) ? (mag | 8u) : mag;
-}
 
 // E4M3FN byte -> float (format definition: bias 7, subnormals m * 2^-9).
 __device__ __forceinline__ float e4m3_value(uint32_t b) {
@@ -67,17 +54,25 @@ __device__ __forceinline__ float amax8(uint4 v) {
   return a;
 }
 
+// Two elements -> one byte of E2M1 codes (low nibble = first element) with
+// the hardware round-to-nearest-even, saturating conversion; NaN is mapped to
+// zero first (the format spec gives NaN code 0).
+__device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
+  lo = (lo == lo) ? lo : 0.0f;
+  hi = (hi == hi) ? hi : 0.0f;
+  return (uint32_t)__nv_cvt_float2_to_fp4x2(make_float2(lo, hi), __NV_E2M1, cudaRoundNearest);
+}
+
+// Eight elements -> 32 bits of codes.  A value that rounds to magnitude 0
+// keeps no sign bit (canonical zero, code 0).
 __device__ __forceinline__ uint32_t pack8(uint4 v, float rs) {
-  uint32_t c = 0;
-  c |= e2m1_code(__fmul_rn(bf16_lo(v.x), rs)) << 0;
-  c |= e2m1_code(__fmul_rn(bf16_hi(v.x), rs)) << 4;
-  c |= e2m1_code(__fmul_rn(bf16_lo(v.y), rs)) << 8;
-  c |= e2m1_code(__fmul_rn(bf16_hi(v.y), rs)) << 12;
-  c |= e2m1_code(__fmul_rn(bf16_lo(v.z), rs)) << 16;
-  c |= e2m1_code(__fmul_rn(bf16_hi(v.z), rs)) << 20;
-  c |= e2m1_code(__fmul_rn(bf16_lo(v.w), rs)) << 24;
-  c |= e2m1_code(__fmul_rn(bf16_hi(v.w), rs)) << 28;
-  return c;
+  uint32_t c = cvt2(__fmul_rn(bf16_lo(v.x), rs), __fmul_rn(bf16_hi(v.x), rs));
+  c |= cvt2(__fmul_rn(bf16_lo(v.y), rs), __fmul_rn(bf16_hi(v.y), rs)) << 8;
+  c |= cvt2(__fmul_rn(bf16_lo(v.z), rs), __fmul_rn(bf16_hi(v.z), rs)) << 16;
+  c |= cvt2(__fmul_rn(bf16_lo(v.w), rs), __fmul_rn(bf16_hi(v.w), rs)) << 24;
+  const uint32_t mag = c & 0x77777777u;
+  const uint32_t nz = (mag | (mag >> 1) | (mag >> 2)) & 0x11111111u;
+  return mag | (c & (nz << 3));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -113,8 +108,34 @@ __global__ void __launch_bounds__(256) amax_kernel(const __nv_bfloat16* __restri
 
 __global__ void finalize_gs_kernel(float* gs) { gs[0] = global_scale(gs[0]); }
 
+// One 8-element chunk of a row: block absmax (lanes 2i, 2i+1), scale, codes,
+// and the 32-bit scale-group store (lanes with lane % 8 == 0).  Every lane of
+// the warp calls this (the shuffles need the full warp); `valid` masks stores.
+__device__ __forceinline__ void quant_chunk(uint4 v, bool valid, int64_t c, int lane, float g, float denom,
+                                            uint32_t* code_row, uint8_t* sf_rowbase) {
+  const float mine = amax8(v);
+  const float am = fmaxf(mine, __shfl_xor_sync(0xffffffffu, mine, 1));
+  const float s = fminf(__fdiv_rn(am, denom), 448.0f);
+  const uint32_t sb = e4m3_rne_sat(s);
+  const float sbf = e4m3_value(sb);
+  uint32_t packed = 0u;
+  if (sbf != 0.0f) packed = pack8(v, __frcp_rn(__fmul_rn(sbf, g)));
+  const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
+  const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
+  const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
+  if (valid) {
+    code_row[c] = packed;
+    if ((lane & 7) == 0)
+      *reinterpret_cast<uint32_t*>(sf_rowbase + ((c >> 1) >> 2) * 512) = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
 // GS_MODE: 0 static (gs[0] is g), 1 dynamic (gs[0] holds amax, g derived), 2 per row.
-template <int GS_MODE>
+// NCH > 0: the row has exactly NCH * 256 elements and is held in registers
+// (all of a lane's 128-bit loads are in flight at once -- enough bytes in
+// flight to run at HBM speed with one warp per row).  NCH == 0: any K % 64 == 0,
+// the row is streamed twice (per-row mode re-reads it from L1/L2).
+template <int GS_MODE, int NCH>
 __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
                                                        int64_t ldx, int64_t Mpad, float* __restrict__ gs,
                                                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
@@ -131,45 +152,58 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __re
     return;
   }
   const uint4* row = reinterpret_cast<const uint4*>(x + m * ldx);
-
-  float g;
-  if (GS_MODE == 0) {
-    g = gs[0];
-  } else if (GS_MODE == 1) {
-    g = global_scale(gs[0]);
-  } else {
-    float a = 0.0f;
-    for (int64_t c = lane; c < nchunk; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
-    g = global_scale(warp_max(a));
-    if (lane == 0) gs[m] = g;
-  }
-  const float denom = __fmul_rn(6.0f, g);
   uint32_t* code_row = reinterpret_cast<uint32_t*>(codes + m * (K / 2));
 
-  // Every lane runs every iteration (shuffles need the full warp); K % 64 == 0
-  // makes the valid lanes of the last iteration whole groups of 8.
-  for (int64_t base = 0; base < nchunk; base += 32) {
-    const int64_t c = base + lane;
-    const bool valid = c < nchunk;
-    const uint4 v = valid ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
-    const float mine = amax8(v);
-    const float am = fmaxf(mine, __shfl_xor_sync(0xffffffffu, mine, 1));
-    const float s = fminf(__fdiv_rn(am, denom), 448.0f);
-    const uint32_t sb = e4m3_rne_sat(s);
-    const float sbf = e4m3_value(sb);
-    uint32_t packed = 0u;
-    if (sbf != 0.0f) packed = pack8(v, __frcp_rn(__fmul_rn(sbf, g)));
-    // block kb = c / 2; lanes with lane % 8 == 0 gather the scales of blocks kb..kb+3
-    const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
-    const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
-    const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
-    if (valid) {
-      code_row[c] = packed;
-      if ((lane & 7) == 0) {
-        const int64_t kb = c >> 1;
-        *reinterpret_cast<uint32_t*>(sf_rowbase + (kb >> 2) * 512) = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
-      }
+  if constexpr (NCH > 0) {
+    uint4 v[NCH];
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) v[j] = __ldg(row + lane + 32 * j);
+    float g;
+    if (GS_MODE == 0) {
+      g = gs[0];
+    } else if (GS_MODE == 1) {
+      g = global_scale(gs[0]);
+    } else {
+      float a = 0.0f;
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) a = fmaxf(a, amax8(v[j]));
+      g = global_scale(warp_max(a));
+      if (lane == 0) gs[m] = g;
     }
+    const float denom = __fmul_rn(6.0f, g);
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, lane + 32 * j, lane, g, denom, code_row, sf_rowbase);
+  } else {
+    float g;
+    if (GS_MODE == 0) {
+      g = gs[0];
+    } else if (GS_MODE == 1) {
+      g = global_scale(gs[0]);
+    } else {
+      float a = 0.0f;
+      for (int64_t c = lane; c < nchunk; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
+      g = global_scale(warp_max(a));
+      if (lane == 0) gs[m] = g;
+    }
+    const float denom = __fmul_rn(6.0f, g);
+    // K % 64 == 0 makes the valid lanes of the last iteration whole groups of 8.
+    for (int64_t base = 0; base < nchunk; base += 32) {
+      const int64_t c = base + lane;
+      const bool valid = c < nchunk;
+      const uint4 v = valid ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
+      quant_chunk(v, valid, c, lane, g, denom, code_row, sf_rowbase);
+    }
+  }
+}
+
+template <int GS_MODE>
+void launch_quantize(dim3 grid, cudaStream_t st, const __nv_bfloat16* x, int64_t M, int64_t K, int64_t ldx,
+                     int64_t Mpad, float* gs, uint8_t* codes, uint8_t* sf) {
+  switch (K) {
+    case 2048: quantize_kernel<GS_MODE, 8><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
+    case 4096: quantize_kernel<GS_MODE, 16><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
+    case 6144: quantize_kernel<GS_MODE, 24><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
+    default: quantize_kernel<GS_MODE, 0><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
   }
 }
 
@@ -198,17 +232,17 @@ extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t
   const dim3 grid((unsigned)((Mpad + kQuantWarps - 1) / kQuantWarps));
   const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   if (gs_mode == DEMON_GS_STATIC) {
-    quantize_kernel<0><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<0>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
   } else if (gs_mode == DEMON_GS_DYNAMIC) {
     DEMON_CUDA(cudaMemsetAsync(gs, 0, sizeof(float), st));
     if (M > 0) {
       const int blocks = (int)std::min<int64_t>((M + kQuantWarps - 1) / kQuantWarps, 148 * 8);
       amax_kernel<<<blocks, 256, 0, st>>>(xb, M, K, ldx, gs);
     }
-    quantize_kernel<1><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<1>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
     finalize_gs_kernel<<<1, 1, 0, st>>>(gs);
   } else {
-    quantize_kernel<2><<<grid, 256, 0, st>>>(xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<2>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
   }
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
