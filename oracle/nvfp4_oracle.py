@@ -199,9 +199,9 @@ def quantize_numpy(x_bf16_bits: np.ndarray, gs_mode: int = GS_PER_ROW, gs=None):
     s = np.where(s <= f32(448.0), s, f32(448.0)).astype(f32)
     sb_bits, sbf = _e4m3_torch(s)
     scale = (sbf * g).astype(f32)
-    with np.errstate(divide="ignore"):
+    with np.errstate(divide="ignore", invalid="ignore"):
         rs = (f32(1.0) / scale).astype(f32)
-    v = (xb * rs[..., None]).astype(f32)
+        v = (xb * rs[..., None]).astype(f32)  # zero-scale blocks give 0*inf here; masked below
     codes = _e2m1_nearest_even(v)
     codes = np.where((sbf == 0)[..., None], np.uint8(0), codes).reshape(M, K)
     packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
