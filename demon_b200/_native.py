@@ -36,7 +36,7 @@ ODE_VS = 1 << 13
 EXPORTED = (
     "demon_abi_version", "demon_struct_sizes", "demon_last_error", "demon_device_status",
     "demon_nvfp4_sf_bytes", "demon_nvfp4_quantize", "demon_nvfp4_gemm", "demon_lora_down",
-    "demon_ode_step", "demon_ode_prepare",
+    "demon_ode_step", "demon_ode_prepare", "demon_nvfp4_noalloc_scratch_bytes", "demon_nvfp4_linear_noalloc",
 )
 
 _vp = ctypes.c_void_p
@@ -114,8 +114,10 @@ def load() -> ctypes.CDLL:
         L.demon_lora_down.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, ctypes.c_int, _vp, _vp, _vp]
         L.demon_ode_step.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
         L.demon_ode_prepare.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
+        L.demon_nvfp4_linear_noalloc.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp]
         for name in EXPORTED:
-            getattr(L, name).restype = _i64 if name == "demon_nvfp4_sf_bytes" else ctypes.c_int
+            getattr(L, name).restype = (_i64 if name in ("demon_nvfp4_sf_bytes", "demon_nvfp4_noalloc_scratch_bytes")
+                                        else ctypes.c_int)
         g, o = _i64(), _i64()
         L.demon_struct_sizes(ctypes.byref(g), ctypes.byref(o))
         if g.value != ctypes.sizeof(DemonGemmArgs) or o.value != ctypes.sizeof(DemonOdeSlot):

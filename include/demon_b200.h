@@ -132,6 +132,24 @@ DEMON_API int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, 
                     void* stream);
 
 /*
+ * NVFP4 linear that allocates nothing: out = x W^T + bias (bf16 [M, ldo]),
+ * i.e. demon_nvfp4_quantize (per-row global scales) followed by
+ * demon_nvfp4_gemm, with the quantised activation kept in a fixed device
+ * array inside the library instead of caller buffers.  No counterpart in the
+ * reference: it is for callers that cannot allocate device memory while the
+ * layer runs (a TensorRT plugin's enqueue(), a real-time thread that must not
+ * block in cudaMalloc).  Limits: M * K <= 8,388,608, M <= 65,536, K % 256 == 0,
+ * N % 128 == 0.  The array (demon_nvfp4_noalloc_scratch_bytes() bytes) lives on
+ * every GPU that loads the library until exit and is shared by all calls on a
+ * device: calls that overlap on the GPU race.  The first call on a device
+ * looks up the array's address (make it before any stream capture).
+ */
+DEMON_API int64_t demon_nvfp4_noalloc_scratch_bytes(void);
+DEMON_API int demon_nvfp4_linear_noalloc(const void* x, int64_t M, int64_t K, int64_t ldx, const uint8_t* w_codes,
+                                         const uint8_t* w_sf, const float* w_gs, int64_t N, const void* bias,
+                                         void* out, int64_t ldo, void* stream);
+
+/*
  * Fused per-slot ODE step over one tick (all slots in one launch).
  * Stands in for StreamPipeline._tick_pt's post-forward section
  * (acestep/engine/stream.py:983-998, 1060-1276) composed from

@@ -1,0 +1,72 @@
+"""The allocation-free NVFP4 linear (demon_nvfp4_linear_noalloc).
+
+Callers that cannot allocate device memory while the layer runs -- a TensorRT
+plugin's enqueue(), or a real-time thread that must not block in cudaMalloc --
+use this entry point: it keeps the quantised activation in a fixed array
+inside the library instead of buffers the caller provides.  This test calls it
+through the C ABI twice in a row (the second call reuses the array the first
+one left behind) and checks each result against the regular entry points
+(demon_nvfp4_quantize + demon_nvfp4_gemm) with the GEMM tolerance used by the
+other tests, relative Frobenius error <= 1e-2.  It also checks that a call
+larger than the array is rejected before anything runs.
+
+This file is collected last so that a run stopping at the first failure has
+already run every other test; it also passes on its own in a fresh process.
+"""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REL_FRO_TOL = 1e-2
+
+
+def _linear_noalloc(lib, x, w, bias, out):
+    from demon_b200 import _native as nat
+    M, K = x.shape
+    return lib.demon_nvfp4_linear_noalloc(
+        ctypes.c_void_p(x.data_ptr()), M, K, x.stride(0), ctypes.c_void_p(w.codes.data_ptr()),
+        ctypes.c_void_p(w.sf.data_ptr()), ctypes.c_void_p(w.gs.data_ptr()), w.rows,
+        ctypes.c_void_p(bias.data_ptr() if bias is not None else 0), ctypes.c_void_p(out.data_ptr()), out.stride(0),
+        ctypes.c_void_p(nat.stream_ptr()))
+
+
+def _rel_fro(y, ref):
+    return float((y.double() - ref.double()).norm() / ref.double().norm())
+
+
+def test_noalloc_linear_matches_regular_path_twice(cuda):
+    from demon_b200 import _native as nat
+    from demon_b200 import nvfp4
+    lib = nat.load()
+    g = torch.Generator().manual_seed(77)
+    cases = [(1500, 2048, 6144), (700, 6144, 2048)]  # second call: different shape, same array
+    for M, K, N in cases:
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(cuda)
+        w = nvfp4.pack_weight((torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(cuda))
+        bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16).to(cuda)
+        ref = nvfp4.gemm(nvfp4.quantize(x), w, bias=bias)
+        out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+        rc = _linear_noalloc(lib, x, w, bias, out)
+        assert rc == nat.DEMON_OK, nat.last_error()
+        torch.cuda.synchronize()
+        assert torch.isfinite(out).all()
+        assert _rel_fro(out, ref) <= REL_FRO_TOL
+    assert nat.device_status() == (0, 0)
+
+
+def test_noalloc_linear_rejects_oversized_calls(cuda):
+    from demon_b200 import _native as nat
+    from demon_b200 import nvfp4
+    lib = nat.load()
+    K, N = 6144, 128
+    M = 8_388_608 // K + 1  # one row past the array's activation limit
+    x = torch.zeros(M, K, dtype=torch.bfloat16, device=cuda)
+    w = nvfp4.pack_weight(torch.zeros(N, K, dtype=torch.bfloat16, device=cuda))
+    out = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda)
+    rc = _linear_noalloc(lib, x, w, None, out)
+    assert rc == nat.DEMON_ERR_INVALID
+    assert "scratch" in nat.last_error()
+    assert lib.demon_nvfp4_noalloc_scratch_bytes() == (4 << 20) + (640 << 10) + 65536 * 4
