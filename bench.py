@@ -181,6 +181,117 @@ def run_reference(args):
 # Our path
 # ---------------------------------------------------------------------------
 
+def ode_workload(dev, nslots=64, T=1500, seed=0):
+    """Config-3 slot features at config-5 scale: 64 slots x T=1500 x 64, CFG modes cycling
+    standard / RCFG-initialize (cached negative) / RCFG-self, per-slot guidance U(3,7),
+    per-frame velocity_scale / sde_denoise / apg_momentum / cfg_rescale splines in [0, 1.5],
+    source latents (SDE-curve path), binary latent mask with 40 % spans, channel gain U(0.8, 1.2).
+    Returns (OdeTick with the slots added, algorithmic bytes per launch, gain)."""
+    import torch
+    from demon_b200 import ode
+    g = torch.Generator().manual_seed(seed)
+    D = 64
+    bf = torch.bfloat16
+
+    def spline(lo, hi):
+        knots = torch.rand(16, generator=g) * (hi - lo) + lo
+        xs = torch.linspace(0, 15, T)
+        i = xs.floor().clamp(max=14).long()
+        f = xs - i
+        return knots[i] * (1 - f) + knots[i + 1] * f
+
+    def lat():
+        return torch.randn(T, D, generator=g).to(bf).to(dev)
+
+    tick = ode.OdeTick(dev, T, max_slots=nslots)
+    vpos = torch.randn(nslots, T, D, generator=g).to(bf).to(dev)
+    vneg = torch.randn(nslots, T, D, generator=g).to(bf).to(dev)
+    gain = (torch.rand(T, D, generator=g) * 0.4 + 0.8).to(bf).to(dev)
+    elems = T * D
+    nbytes = 0
+    for i in range(nslots):
+        mode = ("full", "initialize", "self")[i % 3]
+        m = torch.zeros(T)
+        a = int(torch.randint(0, T - int(0.4 * T), (1,), generator=g))
+        m[a:a + int(0.4 * T)] = 1.0
+        st = ode.SlotStep(
+            xt=lat(), t_curr=0.75, t_next=0.5, step_idx=3, total_steps=8, pos=[(vpos[i], None)],
+            has_cfg=True, rcfg_mode=mode,
+            neg=[(vneg[i], None)] if mode == "full" else None,
+            neg_cached=lat() if mode == "initialize" else None,
+            initial_noise=lat() if mode == "self" else None,
+            momentum=lat(), momentum_fresh=False,
+            guidance=float(torch.rand(1, generator=g)) * 4 + 3, apg_momentum=spline(0, 1.5),
+            cfg_rescale=spline(0, 1.5), velocity_scale=spline(0, 1.5), sde_denoise_curve=spline(0, 1.5),
+            source=lat(), mask=ode.LatentMask(m.to(dev), lat(), lat()),
+            dec_out=torch.empty(T, D, dtype=bf, device=dev), seed=1000 + i)
+        tick.add(st)
+        # reads: v_pos, v_neg source, momentum, xt, mask original + noise, source, gain; writes: momentum, xt, dec
+        nbytes += elems * 2 * (8 + 3)
+    return tick, nbytes, gain
+
+
+def measure_ode(dev, stream, reps=20):
+    """HBM roofline of the fused ODE step: two slot sets (2 x 135 MB > 2x L2) alternated."""
+    import torch
+    from demon_b200 import _native as nat
+    ticks = [ode_workload(dev, seed=s) for s in (0, 1)]
+    launches = []
+    for tk, nbytes, gain in ticks:
+        b, nb = tk._stage()
+        tk._dev[b][:nb].copy_(tk._host[b][:nb])
+        launches.append((tk._dev[b].data_ptr(), len(tk.slots), tk.T, nbytes, gain))
+    torch.cuda.synchronize()
+
+    def run(i):
+        ptr, n, T, _, gain = launches[i % 2]
+        nat.check(nat.load().demon_ode_step(ptr, n, T, 64, nat.ptr(gain), int(stream.cuda_stream)))
+
+    for i in range(4):
+        run(i)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for i in range(reps):
+            run(i)
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    gr.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    nbytes = sum(l[3] for l in launches) / 2
+    return {"kernel": "demon::ode_step_kernel", "workload": "64 slots x T=1500 x 64 (config-3 features)",
+            "us": us, "bytes": nbytes, "achieved": nbytes / (us * 1e-6) / 1e9, "unit": "GB/s"}
+
+
+def measure_quantize(sets, stream, reps=8):
+    import torch
+    from demon_b200 import nvfp4
+    nsets = len(sets)
+    for s_ in sets:
+        nvfp4.quantize(s_["x"])
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(reps):
+            for s_ in sets:
+                nvfp4.quantize(s_["x"])
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    gr.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * nsets)
+    nbytes = M1 * K1 * 2 + M1 * K1 // 2 + M1 * K1 // 16
+    return {"kernel": "demon::quantize_rows_kernel<2,2>", "workload": "x bf16 [1500, 2048], per-row scales",
+            "us": us, "bytes": nbytes, "achieved": nbytes / (us * 1e-6) / 1e9, "unit": "GB/s"}
+
+
 def run_linear(args):
     import torch
     rank, world, local = env_rank()
@@ -260,6 +371,8 @@ def run_linear(args):
     torch.cuda.synchronize()
     ms = max_over_ranks(ms_local, dist_mod, dev)
     gemm_avg = max_over_ranks(g0.elapsed_time(g1) / (gemm_reps * nsets), dist_mod, dev)
+    quant = measure_quantize(sets, stream)
+    odek = measure_ode(dev, stream) if args.ode else None
     status = nat.device_status()
 
     # end to end through the public API: pinned host x -> device, NVFP4Linear, y -> pinned host
@@ -310,6 +423,10 @@ def run_linear(args):
             "clocks": clk.summary(),
             "device_status": list(status),
         }
+        kern = {"quantize": dict(quant, peak=pk["hbm_gbs"], frac=quant["achieved"] / pk["hbm_gbs"])}
+        if odek is not None:
+            kern["ode_step"] = dict(odek, peak=pk["hbm_gbs"], frac=odek["achieved"] / pk["hbm_gbs"])
+        line["kernels"] = kern
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -326,6 +443,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="linear", choices=["linear"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-ode", dest="ode", action="store_false", help="skip the ODE-step roofline leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -131,11 +131,9 @@ __device__ __forceinline__ void quant_chunk(uint4 v, bool valid, int64_t c, int 
 }
 
 // GS_MODE: 0 static (gs[0] is g), 1 dynamic (gs[0] holds amax, g derived), 2 per row.
-// NCH > 0: the row has exactly NCH * 256 elements and is held in registers
-// (all of a lane's 128-bit loads are in flight at once -- enough bytes in
-// flight to run at HBM speed with one warp per row).  NCH == 0: any K % 64 == 0,
-// the row is streamed twice (per-row mode re-reads it from L1/L2).
-template <int GS_MODE, int NCH>
+// Generic path (any K % 64 == 0): one warp per row, the row streamed in
+// 32-chunk steps (per-row mode reads it twice, the second time from L1/L2).
+template <int GS_MODE>
 __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
                                                        int64_t ldx, int64_t Mpad, float* __restrict__ gs,
                                                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
@@ -146,64 +144,105 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __re
   const int64_t kchunks64 = K / 64;  // scale chunks per 128-row block
   const int64_t r = m & 127;
   uint8_t* sf_rowbase = sf + (m >> 7) * kchunks64 * 512 + (r & 31) * 16 + (r >> 5) * 4;
-
   if (m >= M) {  // padding rows of the scale layout: zero scales
     for (int64_t c = lane; c < K / 64; c += 32) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
     return;
   }
   const uint4* row = reinterpret_cast<const uint4*>(x + m * ldx);
   uint32_t* code_row = reinterpret_cast<uint32_t*>(codes + m * (K / 2));
-
-  if constexpr (NCH > 0) {
-    uint4 v[NCH];
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) v[j] = __ldg(row + lane + 32 * j);
-    float g;
-    if (GS_MODE == 0) {
-      g = gs[0];
-    } else if (GS_MODE == 1) {
-      g = global_scale(gs[0]);
-    } else {
-      float a = 0.0f;
-#pragma unroll
-      for (int j = 0; j < NCH; ++j) a = fmaxf(a, amax8(v[j]));
-      g = global_scale(warp_max(a));
-      if (lane == 0) gs[m] = g;
-    }
-    const float denom = __fmul_rn(6.0f, g);
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, lane + 32 * j, lane, g, denom, code_row, sf_rowbase);
+  float g;
+  if (GS_MODE == 0) {
+    g = gs[0];
+  } else if (GS_MODE == 1) {
+    g = global_scale(gs[0]);
   } else {
-    float g;
-    if (GS_MODE == 0) {
-      g = gs[0];
-    } else if (GS_MODE == 1) {
-      g = global_scale(gs[0]);
-    } else {
-      float a = 0.0f;
-      for (int64_t c = lane; c < nchunk; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
-      g = global_scale(warp_max(a));
-      if (lane == 0) gs[m] = g;
-    }
-    const float denom = __fmul_rn(6.0f, g);
-    // K % 64 == 0 makes the valid lanes of the last iteration whole groups of 8.
-    for (int64_t base = 0; base < nchunk; base += 32) {
-      const int64_t c = base + lane;
-      const bool valid = c < nchunk;
-      const uint4 v = valid ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
-      quant_chunk(v, valid, c, lane, g, denom, code_row, sf_rowbase);
-    }
+    float a = 0.0f;
+    for (int64_t c = lane; c < nchunk; c += 32) a = fmaxf(a, amax8(__ldg(row + c)));
+    g = global_scale(warp_max(a));
+    if (lane == 0) gs[m] = g;
+  }
+  const float denom = __fmul_rn(6.0f, g);
+  // K % 64 == 0 makes the valid lanes of the last iteration whole groups of 8.
+  for (int64_t base = 0; base < nchunk; base += 32) {
+    const int64_t c = base + lane;
+    const bool valid = c < nchunk;
+    const uint4 v = valid ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
+    quant_chunk(v, valid, c, lane, g, denom, code_row, sf_rowbase);
   }
 }
 
+// Fast path for K = NCH * 1024: a row is split over kRowWarps warps (each lane
+// holds NCH 128-bit chunks in registers, all loads in flight at once); the
+// per-row absmax is combined through shared memory.  Two rows per 256-thread CTA.
+constexpr int kRowWarps = 4;
+template <int GS_MODE, int NCH>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t M,
+                                                            int64_t ldx, int64_t Mpad, float* __restrict__ gs,
+                                                            uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  constexpr int64_t K = (int64_t)NCH * 1024;
+  constexpr int kRowsPerCta = 8 / kRowWarps;
+  __shared__ float red[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wr = warp % kRowWarps;
+  const int64_t m = (int64_t)blockIdx.x * kRowsPerCta + warp / kRowWarps;
+  const int64_t r = m & 127;
+  uint8_t* sf_rowbase = sf + (m >> 7) * (K / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
+  const bool pad = m >= M;
+  const uint4* row = reinterpret_cast<const uint4*>(x + (pad ? 0 : m) * ldx);
+  uint32_t* code_row = reinterpret_cast<uint32_t*>(codes + (pad ? 0 : m) * (K / 2));
+  const int64_t cbase = (int64_t)wr * 32 * NCH;  // this warp's first 8-element chunk
+  uint4 v[NCH];
+  if (!pad) {
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) v[j] = __ldg(row + cbase + 32 * j + lane);
+  }
+  float g = 0.0f;
+  if (GS_MODE == 0) {
+    g = gs[0];
+  } else if (GS_MODE == 1) {
+    g = global_scale(gs[0]);
+  } else {
+    float a = 0.0f;
+    if (!pad) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) a = fmaxf(a, amax8(v[j]));
+    }
+    a = warp_max(a);
+    if (lane == 0) red[warp] = a;
+    __syncthreads();
+    const int w0 = warp - wr;
+    float am = red[w0];
+#pragma unroll
+    for (int i = 1; i < kRowWarps; ++i) am = fmaxf(am, red[w0 + i]);
+    g = global_scale(am);
+    if (wr == 0 && lane == 0 && !pad) gs[m] = g;
+  }
+  if (m >= Mpad) return;
+  if (pad) {  // padding rows of the scale layout: zero scales
+    for (int64_t c = wr * 32 + lane; c < K / 64; c += 32 * kRowWarps)
+      *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+    return;
+  }
+  const float denom = __fmul_rn(6.0f, g);
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, cbase + 32 * j + lane, lane, g, denom, code_row, sf_rowbase);
+}
+
 template <int GS_MODE>
-void launch_quantize(dim3 grid, cudaStream_t st, const __nv_bfloat16* x, int64_t M, int64_t K, int64_t ldx,
-                     int64_t Mpad, float* gs, uint8_t* codes, uint8_t* sf) {
+void launch_quantize(cudaStream_t st, const __nv_bfloat16* x, int64_t M, int64_t K, int64_t ldx, int64_t Mpad,
+                     float* gs, uint8_t* codes, uint8_t* sf) {
+  const dim3 grid_rows((unsigned)((Mpad + 1) / 2));  // two rows per CTA
   switch (K) {
-    case 2048: quantize_kernel<GS_MODE, 8><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
-    case 4096: quantize_kernel<GS_MODE, 16><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
-    case 6144: quantize_kernel<GS_MODE, 24><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
-    default: quantize_kernel<GS_MODE, 0><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf); break;
+    case 1024: quantize_rows_kernel<GS_MODE, 1><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 2048: quantize_rows_kernel<GS_MODE, 2><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 3072: quantize_rows_kernel<GS_MODE, 3><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 4096: quantize_rows_kernel<GS_MODE, 4><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 6144: quantize_rows_kernel<GS_MODE, 6><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 8192: quantize_rows_kernel<GS_MODE, 8><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    default: {
+      const dim3 grid((unsigned)((Mpad + kQuantWarps - 1) / kQuantWarps));
+      quantize_kernel<GS_MODE><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf);
+    }
   }
 }
 
@@ -229,20 +268,19 @@ extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t Mpad = (M + 127) / 128 * 128;
   if (Mpad == 0) return DEMON_OK;
-  const dim3 grid((unsigned)((Mpad + kQuantWarps - 1) / kQuantWarps));
   const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   if (gs_mode == DEMON_GS_STATIC) {
-    launch_quantize<0>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<0>(st, xb, M, K, ldx, Mpad, gs, codes, sf);
   } else if (gs_mode == DEMON_GS_DYNAMIC) {
     DEMON_CUDA(cudaMemsetAsync(gs, 0, sizeof(float), st));
     if (M > 0) {
       const int blocks = (int)std::min<int64_t>((M + kQuantWarps - 1) / kQuantWarps, 148 * 8);
       amax_kernel<<<blocks, 256, 0, st>>>(xb, M, K, ldx, gs);
     }
-    launch_quantize<1>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<1>(st, xb, M, K, ldx, Mpad, gs, codes, sf);
     finalize_gs_kernel<<<1, 1, 0, st>>>(gs);
   } else {
-    launch_quantize<2>(grid, st, xb, M, K, ldx, Mpad, gs, codes, sf);
+    launch_quantize<2>(st, xb, M, K, ldx, Mpad, gs, codes, sf);
   }
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
