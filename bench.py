@@ -245,7 +245,7 @@ def measure_ode(dev, stream, reps=20):
 
     def run(i):
         ptr, n, T, _, gain = launches[i % 2]
-        nat.check(nat.load().demon_ode_step(ptr, n, T, 64, nat.ptr(gain), int(stream.cuda_stream)))
+        nat.check(nat.load().demon_ode_step(ptr, n, T, 64, nat.ptr(gain), nat.stream_ptr()))
 
     for i in range(4):
         run(i)

@@ -49,12 +49,13 @@ struct GemmParams {
   const float* col_scale;  // bf16 mode: per-output-column scale
   const __nv_bfloat16* bias;
   const __nv_bfloat16* gate;
+  const __nv_bfloat16* residual;
+  __nv_bfloat16* out;
   unsigned int* status;
-  int64_t gate_rows, ld_gate;
+  int64_t gate_rows, ld_gate, ldo, ldr;
   int M, N, K;
   int a_gs_per_row;
   int lora_rank;
-  int has_residual;
   int m_tiles, n_tiles;
 };
 
@@ -62,7 +63,8 @@ constexpr int kBM = 128;
 constexpr int kRowBytes = 128;   // one 128-byte swizzle row per stage (256 fp4 / 64 bf16)
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kStageBuf = 2048;  // 32 rows x 32 bf16, 64-byte swizzle
+constexpr int kStgPitch = 80;     // staging row pitch: 32 bf16 + 16 bytes of padding (conflict-free)
+constexpr int kStageBuf = 32 * kStgPitch;
 
 template <int BN, int STAGES, bool FP4>
 struct GemmCfg {
@@ -75,8 +77,9 @@ struct GemmCfg {
   static constexpr int offSFA = offB + STAGES * kB;
   static constexpr int offSFB = offSFA + STAGES * kSFA;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
-  static constexpr int offBar = offStg + kEpiWarps * 2 * kStageBuf;
-  static constexpr int kBars = 2 * STAGES + 3 + 2 * kEpiWarps;
+  static constexpr int offBias = offStg + kEpiWarps * kStageBuf;
+  static constexpr int offBar = offBias + kEpiWarps * (BN / 2) * 2;
+  static constexpr int kBars = 2 * STAGES + 3;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
   static constexpr int kSfaCol = BN;                 // 4 columns per K=64 step, 4 steps
@@ -107,7 +110,6 @@ template <int BN, int STAGES, bool FP4>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                 const GemmParams p) {
   using C = GemmCfg<BN, STAGES, FP4>;
   extern __shared__ uint8_t smem_raw[];
@@ -117,7 +119,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
-  uint64_t* res_full = mma_done + 1;  // [kEpiWarps][2]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::offMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::offMisc + 4);
 
@@ -135,19 +136,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, kEpiWarps);
     mbar_init(mma_done, 1);
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    prefetch_tmap(&tmOut);
     if (lboxes) {
       prefetch_tmap(&tmLA);
       prefetch_tmap(&tmLB);
     }
-    if (p.has_residual) prefetch_tmap(&tmRes);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::kTmemCols);
@@ -273,12 +271,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;            // 0..7
     const int q = warp & 3;             // TMEM lane quadrant accessible to this warp
     const int half = ew >> 2;           // which half of the tile's columns
-    uint8_t* stg = smem + C::offStg + ew * 2 * kStageBuf;
-    uint64_t* rbar = res_full + ew * 2;
-    uint32_t it = 0, nchunk = 0;
+    uint8_t* stg = smem + C::offStg + ew * kStageBuf;
+    __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(smem + C::offBias) + ew * (BN / 2);
+    // transposed position of this lane: 8 rows x 4 granules of 16 bytes per pass
+    const int trow = lane >> 2, tgr = lane & 3;
+    uint32_t it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
       const int m0 = m_blk * kBM, n0 = n_blk * BN;
+      const int ncol0 = n0 + half * C::kColsPerWarp;
+      // stage this warp's bias columns while the MMAs run
+      if (FP4) {
+        for (int i = lane; i < C::kColsPerWarp / 8; i += 32) {
+          uint4 bb = make_uint4(0u, 0u, 0u, 0u);
+          if (p.bias && ncol0 + i * 8 < p.N) bb = __ldg(reinterpret_cast<const uint4*>(p.bias + ncol0) + i);
+          reinterpret_cast<uint4*>(bias_s)[i] = bb;
+        }
+      }
+      __syncwarp();
       if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7)) break;
       tc_fence_after();
       if (*abort_flag) break;
@@ -297,84 +307,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float ga = row_ok ? p.a_gs[p.a_gs_per_row ? row : 0] : 0.0f;
       const float alpha = ga * p.w_gs[0];
       const float inv_alpha = FP4 ? 0.0f : (row_ok ? 1.0f / alpha : 0.0f);
-      const __nv_bfloat16* gate_row = (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate : nullptr;
 #pragma unroll
-      for (int c = 0; c < C::kChunks; ++c, ++nchunk) {
-        const int ncol = n0 + half * C::kColsPerWarp + c * 32;
+      for (int c = 0; c < C::kChunks; ++c) {
+        const int ncol = ncol0 + c * 32;
         if (ncol >= p.N) break;  // uniform across the warp
-        uint8_t* buf = stg + (nchunk & 1) * kStageBuf;
-        uint64_t* rb = rbar + (nchunk & 1);
-        // the TMA store that last read this buffer (two chunks ago) must be done reading
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        if (FP4 && p.has_residual) {
-          if (lane == 0) {
-            mbar_arrive_expect_tx(rb, kStageBuf);
-            tma_load_2d(buf, &tmRes, rb, ncol, m0 + q * 32);
-          }
-          mbar_wait(rb, (nchunk >> 1) & 1u, abort_flag, t0, p.status, 8);
-        }
-        float y[32];
+        // row domain: y = alpha * acc + bias (bf16), one row per lane
+        uint32_t w[16];
         if (FP4) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            uint4 bb = make_uint4(0u, 0u, 0u, 0u);
-            if (p.bias) bb = __ldg(reinterpret_cast<const uint4*>(p.bias + ncol) + j);
+            const uint4 bb = reinterpret_cast<const uint4*>(bias_s + c * 32)[j];
             const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              y[8 * j + 2 * i] = fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i]), bf16_lo(bw[i]));
-              y[8 * j + 2 * i + 1] = fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i + 1]), bf16_hi(bw[i]));
-            }
-          }
-          if (gate_row) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 gg = *reinterpret_cast<const uint4*>(gate_row + ncol + 8 * j);
-              const uint32_t gw[4] = {gg.x, gg.y, gg.z, gg.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                y[8 * j + 2 * i] *= bf16_lo(gw[i]);
-                y[8 * j + 2 * i + 1] *= bf16_hi(gw[i]);
-              }
-            }
-          }
-          if (p.has_residual) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 rr = *reinterpret_cast<const uint4*>(buf + stg_off(lane, j));
-              const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                y[8 * j + 2 * i] += bf16_lo(rw[i]);
-                y[8 * j + 2 * i + 1] += bf16_hi(rw[i]);
-              }
-            }
+            for (int i = 0; i < 4; ++i)
+              w[4 * j + i] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i]), bf16_lo(bw[i])),
+                                         fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i + 1]), bf16_hi(bw[i])));
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            y[i] = (ncol + i < p.N) ? __uint_as_float(v[c][i]) * (p.col_scale[ncol + i] * inv_alpha) : 0.0f;
+          for (int i = 0; i < 16; ++i) {
+            const int n0c = ncol + 2 * i;
+            const float s0 = (n0c < p.N) ? p.col_scale[n0c] * inv_alpha : 0.0f;
+            const float s1 = (n0c + 1 < p.N) ? p.col_scale[n0c + 1] * inv_alpha : 0.0f;
+            w[i] = pack_bf16x2(__uint_as_float(v[c][2 * i]) * s0, __uint_as_float(v[c][2 * i + 1]) * s1);
+          }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 o;
-          o.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
-          o.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
-          o.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
-          o.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
-          *reinterpret_cast<uint4*>(buf + stg_off(lane, j)) = o;
-        }
-        fence_proxy_async_smem();
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(stg + lane * kStgPitch + j * 16) =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
         __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmOut, buf, ncol, m0 + q * 32);
-          bulk_commit();
+        // transposed: lane covers rows trow + 8 s, columns ncol + 8 tgr .. +7
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp) {
+          const int rl = trow + 8 * sp;
+          const int64_t grow = (int64_t)m0 + q * 32 + rl;
+          uint4 o = *reinterpret_cast<const uint4*>(stg + rl * kStgPitch + tgr * 16);
+          const int cc = ncol + tgr * 8;
+          if (grow < p.M && cc < p.N) {
+            if (FP4 && (p.gate || p.residual)) {
+              uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+              if (p.gate) {  // y = bf16(y * gate), as the reference's eager `y * gate`
+                const uint4 gg = *reinterpret_cast<const uint4*>(p.gate + (grow / p.gate_rows) * p.ld_gate + cc);
+                const uint32_t gw[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  ow[i] = pack_bf16x2(bf16_lo(ow[i]) * bf16_lo(gw[i]), bf16_hi(ow[i]) * bf16_hi(gw[i]));
+              }
+              if (p.residual) {  // out = bf16(residual + y)
+                const uint4 rr = *reinterpret_cast<const uint4*>(p.residual + grow * p.ldr + cc);
+                const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  ow[i] = pack_bf16x2(bf16_lo(rw[i]) + bf16_lo(ow[i]), bf16_hi(rw[i]) + bf16_hi(ow[i]));
+              }
+              o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
+            *reinterpret_cast<uint4*>(p.out + grow * p.ldo + cc) = o;
+          }
         }
+        __syncwarp();
       }
     }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
   }
 
   tc_fence_before();
@@ -387,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool FP4>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                const CUtensorMap& out, const CUtensorMap& res, GemmParams p, cudaStream_t st) {
+                GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, FP4>;
   auto kern = gemm_kernel<BN, STAGES, FP4>;
   static std::atomic<uint64_t> attr_done{0};
@@ -402,7 +396,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   p.n_tiles = (p.N + BN - 1) / BN;
   const int tiles = p.m_tiles * p.n_tiles;
   const dim3 grid((unsigned)std::min(tiles, sms));
-  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, out, res, p);
+  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, p);
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
 }
@@ -446,19 +440,13 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
 
   const bool bn256 = (N % 256 == 0);
   const uint32_t BN = bn256 ? 256 : 128;
-  CUtensorMap ta, tb, tla, tlb, tout, tres;
+  CUtensorMap ta, tb, tla, tlb;
   memset(&tla, 0, sizeof tla);
   memset(&tlb, 0, sizeof tlb);
-  memset(&tres, 0, sizeof tres);
   DEMON_RC(make_tmap_2d(&ta, a->a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)M,
                         (uint64_t)K / 2, 128, 128));
   DEMON_RC(make_tmap_2d(&tb, a->w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)N,
                         (uint64_t)K / 2, 128, BN));
-  DEMON_RC(make_tmap_2d(&tout, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
-                        (uint64_t)a->ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
-  if (a->residual)
-    DEMON_RC(make_tmap_2d(&tres, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
-                          (uint64_t)a->ldr * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   if (lora) {
     const uint64_t r = (uint64_t)a->lora_rank;
     DEMON_RC(make_tmap_2d(&tla, a->lora_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)M, r * 2, 64, 128));
@@ -471,6 +459,10 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.w_gs = a->w_gs;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(a->bias);
   p.gate = reinterpret_cast<const __nv_bfloat16*>(a->gate);
+  p.residual = reinterpret_cast<const __nv_bfloat16*>(a->residual);
+  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.ldr = a->ldr;
   p.status = status_word();
   p.gate_rows = a->gate_rows > 0 ? a->gate_rows : 1;
   p.ld_gate = a->ld_gate;
@@ -479,10 +471,9 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.K = (int)K;
   p.a_gs_per_row = a->a_gs_per_row;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
-  p.has_residual = a->residual != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, tout, tres, p, st);
-  return launch_gemm<128, 5, true>(ta, tb, tla, tlb, tout, tres, p, st);
+  if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, p, st);
+  return launch_gemm<128, 5, true>(ta, tb, tla, tlb, p, st);
 }
 
 extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* lora_a, int64_t rank,
@@ -496,16 +487,16 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   DEMON_CHECK_ARG(x && lora_a && col_scale && a_gs && w_gs && xa, "lora_down: null pointer");
   DEMON_CHECK_ARG(((uintptr_t)xa & 15) == 0, "lora_down: xa must be 16-byte aligned");
   if (M == 0) return DEMON_OK;
-  CUtensorMap ta, tb, tz, tout;
+  CUtensorMap ta, tb, tz;
   memset(&tz, 0, sizeof tz);
   DEMON_RC(make_tmap_2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64,
                         128));
-  DEMON_RC(make_tmap_2d(&tout, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)rank, (uint64_t)M,
-                        (uint64_t)rank * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   GemmParams p{};
   p.a_gs = a_gs;
   p.w_gs = w_gs;
   p.col_scale = col_scale;
+  p.out = reinterpret_cast<__nv_bfloat16*>(xa);
+  p.ldo = rank;
   p.status = status_word();
   p.M = (int)M;
   p.N = (int)rank;
@@ -515,9 +506,9 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   if (rank <= 64) {
     DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                           (uint64_t)K * 2, 64, 64));
-    return launch_gemm<64, 6, false>(ta, tb, tz, tz, tout, tz, p, st);
+    return launch_gemm<64, 6, false>(ta, tb, tz, tz, p, st);
   }
   DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                         (uint64_t)K * 2, 64, 128));
-  return launch_gemm<128, 6, false>(ta, tb, tz, tz, tout, tz, p, st);
+  return launch_gemm<128, 6, false>(ta, tb, tz, tz, p, st);
 }

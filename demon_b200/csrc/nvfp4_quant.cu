@@ -42,16 +42,20 @@ __device__ __forceinline__ float global_scale(float amax) {
   return __fdiv_rn(fmaxf(amax, 1e-12f), 2688.0f);
 }
 
+// Block absmax of 8 bf16 values with packed bf16x2 abs/max (exact: no rounding).
 __device__ __forceinline__ float amax8(uint4 v) {
-  float a = fabsf(bf16_lo(v.x));
-  a = fmaxf(a, fabsf(bf16_hi(v.x)));
-  a = fmaxf(a, fabsf(bf16_lo(v.y)));
-  a = fmaxf(a, fabsf(bf16_hi(v.y)));
-  a = fmaxf(a, fabsf(bf16_lo(v.z)));
-  a = fmaxf(a, fabsf(bf16_hi(v.z)));
-  a = fmaxf(a, fabsf(bf16_lo(v.w)));
-  a = fmaxf(a, fabsf(bf16_hi(v.w)));
-  return a;
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+
+// Packed fp32 multiply (two IEEE round-to-nearest products per instruction).
+__device__ __forceinline__ float2 mul2(float2 a, float b) {
+  uint64_t r;
+  const uint64_t av = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
+  const uint64_t bv = (uint64_t)__float_as_uint(b) | ((uint64_t)__float_as_uint(b) << 32);
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(av), "l"(bv));
+  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
 }
 
 // Two elements -> one byte of E2M1 codes (low nibble = first element) with
@@ -65,11 +69,12 @@ __device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
 
 // Eight elements -> 32 bits of codes.  A value that rounds to magnitude 0
 // keeps no sign bit (canonical zero, code 0).
+__device__ __forceinline__ uint32_t pack2(uint32_t w, float rs) {
+  const float2 p = mul2(make_float2(bf16_lo(w), bf16_hi(w)), rs);
+  return cvt2(p.x, p.y);
+}
 __device__ __forceinline__ uint32_t pack8(uint4 v, float rs) {
-  uint32_t c = cvt2(__fmul_rn(bf16_lo(v.x), rs), __fmul_rn(bf16_hi(v.x), rs));
-  c |= cvt2(__fmul_rn(bf16_lo(v.y), rs), __fmul_rn(bf16_hi(v.y), rs)) << 8;
-  c |= cvt2(__fmul_rn(bf16_lo(v.z), rs), __fmul_rn(bf16_hi(v.z), rs)) << 16;
-  c |= cvt2(__fmul_rn(bf16_lo(v.w), rs), __fmul_rn(bf16_hi(v.w), rs)) << 24;
+  const uint32_t c = pack2(v.x, rs) | (pack2(v.y, rs) << 8) | (pack2(v.z, rs) << 16) | (pack2(v.w, rs) << 24);
   const uint32_t mag = c & 0x77777777u;
   const uint32_t nz = (mag | (mag >> 1) | (mag >> 2)) & 0x11111111u;
   return mag | (c & (nz << 3));
