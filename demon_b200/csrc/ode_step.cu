@@ -156,11 +156,24 @@ __device__ __forceinline__ void write_dec(const DemonOdeSlot& S, const __nv_bflo
   st4(S.dec_out, off, d);
 }
 
-__global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
+__device__ __forceinline__ void unpack4(uint2 u, float (&v)[4]) {
+  v[0] = bf16_lo(u.x);
+  v[1] = bf16_hi(u.x);
+  v[2] = bf16_lo(u.y);
+  v[3] = bf16_hi(u.y);
+}
+__device__ __forceinline__ uint2 ldraw(const void* p, int64_t off) {
+  return *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + off);
+}
+
+constexpr int kRB = 4;  // rows per batch and thread: all loads of a batch are issued before its compute
+
+__global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
                                                                const __nv_bfloat16* __restrict__ gain,
                                                                int prepare_only) {
   extern __shared__ __align__(16) uint8_t ode_smem[];
   OdeShared& sh = *reinterpret_cast<OdeShared*>(ode_smem);
+  __shared__ __align__(16) DemonOdeSlot s_slot;
   __nv_bfloat16* vp_s = reinterpret_cast<__nv_bfloat16*>(ode_smem + sizeof(OdeShared));
   const int Tc = (T + kOdeCluster - 1) / kOdeCluster;
   __nv_bfloat16* r_s = vp_s + (size_t)Tc * kOdeD;
@@ -168,10 +181,17 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int slot_id = blockIdx.x / kOdeCluster;
-  const DemonOdeSlot& S = slots[slot_id];
+  const int tid = threadIdx.x, cgp = tid & 15, rg = tid >> 4;
+  // the slot descriptor, once per CTA, into shared memory
+  {
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(slots + slot_id);
+    uint64_t* dst = reinterpret_cast<uint64_t*>(&s_slot);
+    for (int i = tid; i < (int)(sizeof(DemonOdeSlot) / 8); i += kOdeThreads) dst[i] = __ldg(src + i);
+  }
+  __syncthreads();
+  const DemonOdeSlot& S = s_slot;
   const int flags = S.flags;
   const int t0 = crank * Tc, t1 = min(T, t0 + Tc);
-  const int tid = threadIdx.x, cgp = tid & 15, rg = tid >> 4;
   const int c0 = cgp * 4;
 
   if (prepare_only) {
@@ -187,6 +207,9 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
   }
 
   const bool cfg = (flags & DEMON_ODE_CFG) != 0;
+  const bool mom_init = (flags & DEMON_ODE_MOM_INIT) != 0;
+  const bool cache_neg = (flags & DEMON_ODE_CACHE_NEG) != 0;
+  const int n_pos = S.n_pos, n_neg = S.n_neg;
 
   // ---------------- phase 1: velocity assembly, momentum, moments ----------
   float mom[8][4];
@@ -195,36 +218,53 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
 #pragma unroll
     for (int j = 0; j < 4; ++j) mom[i][j] = 0.f;
 
-  for (int t = t0 + rg; t < t1; t += 16) {
-    const int64_t off = (int64_t)t * kOdeD + c0;
-    const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
-    float vp[4];
-    blend(S.v_pos, S.w_pos, S.n_pos, off, t, vp);
-    st4(vp_s, loc, vp);
-    if (cfg) {
-      float vn[4], ro[4] = {0.f, 0.f, 0.f, 0.f}, r[4];
-      blend(S.v_neg, S.w_neg, S.n_neg, off, t, vn);
-      if (flags & DEMON_ODE_CACHE_NEG) st4(S.neg_cache, off, vn);
-      if (!(flags & DEMON_ODE_MOM_INIT)) ld4(S.momentum, off, ro);
-      const float mt = rnd(curve(S.apg_mom, S.apg_mom_s, t));
+  for (int tb = t0 + rg; tb < t1; tb += 16 * kRB) {
+    uint2 up[kRB], un[kRB], uo[kRB];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) r[j] = (flags & DEMON_ODE_MOM_INIT) ? rnd(vp[j] - vn[j])
-                                                                     : rnd(rnd(vp[j] - vn[j]) + rnd(mt * ro[j]));
-      st4(S.momentum, off, r);
-      st4(r_s, loc, r);
-      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
-      const float w2 = w * w;
+    for (int i = 0; i < kRB; ++i) {
+      const int t = min(tb + 16 * i, t1 - 1);  // clamped: rows past t1 load a valid row, never stored
+      const int64_t off = (int64_t)t * kOdeD + c0;
+      up[i] = n_pos <= 1 ? ldraw(S.v_pos[0], off) : make_uint2(0u, 0u);
+      if (cfg) {
+        un[i] = n_neg <= 1 ? ldraw(S.v_neg[0], off) : make_uint2(0u, 0u);
+        uo[i] = mom_init ? make_uint2(0u, 0u) : ldraw(S.momentum, off);
+      }
+    }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float pp = vp[j] * vp[j], pr = vp[j] * r[j], rr = r[j] * r[j];
-        mom[0][j] += rr;
-        mom[1][j] += pp;
-        mom[2][j] += pr;
-        mom[3][j] = fmaf(w, pp, mom[3][j]);
-        mom[4][j] = fmaf(w2, pp, mom[4][j]);
-        mom[5][j] = fmaf(w, pr, mom[5][j]);
-        mom[6][j] = fmaf(w2, pr, mom[6][j]);
-        mom[7][j] = fmaf(w2, rr, mom[7][j]);
+    for (int i = 0; i < kRB; ++i) {
+      const int t = tb + 16 * i;
+      if (t >= t1) break;
+      const int64_t off = (int64_t)t * kOdeD + c0;
+      const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
+      float vp[4];
+      if (n_pos <= 1) unpack4(up[i], vp);
+      else blend(S.v_pos, S.w_pos, n_pos, off, t, vp);
+      st4(vp_s, loc, vp);
+      if (cfg) {
+        float vn[4], ro[4], r[4];
+        if (n_neg <= 1) unpack4(un[i], vn);
+        else blend(S.v_neg, S.w_neg, n_neg, off, t, vn);
+        if (cache_neg) st4(S.neg_cache, off, vn);
+        unpack4(uo[i], ro);
+        const float mt = rnd(curve(S.apg_mom, S.apg_mom_s, t));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = mom_init ? rnd(vp[j] - vn[j]) : rnd(rnd(vp[j] - vn[j]) + rnd(mt * ro[j]));
+        st4(S.momentum, off, r);
+        st4(r_s, loc, r);
+        const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
+        const float w2 = w * w;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float pp = vp[j] * vp[j], pr = vp[j] * r[j], rr = r[j] * r[j];
+          mom[0][j] += rr;
+          mom[1][j] += pp;
+          mom[2][j] += pr;
+          mom[3][j] = fmaf(w, pp, mom[3][j]);
+          mom[4][j] = fmaf(w2, pp, mom[4][j]);
+          mom[5][j] = fmaf(w, pr, mom[5][j]);
+          mom[6][j] = fmaf(w2, pr, mom[6][j]);
+          mom[7][j] = fmaf(w2, rr, mom[7][j]);
+        }
       }
     }
   }
@@ -242,9 +282,9 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
     __syncthreads();
     for (int e = tid; e < 16 * 32; e += kOdeThreads) {
       const int g = e >> 5, q = e & 31;  // channel group, (moment, channel-in-group)
-      double s = 0.0;
-      for (int w = 0; w < kOdeThreads / 32; ++w) s += (double)sh.warp_part[w][g][q];
-      sh.cta_part[g * 4 + (q & 3)][q >> 2] = s;
+      double sacc = 0.0;
+      for (int w = 0; w < kOdeThreads / 32; ++w) sacc += (double)sh.warp_part[w][g][q];
+      sh.cta_part[g * 4 + (q & 3)][q >> 2] = sacc;
     }
   }
   cluster.sync();  // partial moments of every CTA are visible cluster-wide
@@ -278,7 +318,13 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
   const bool final_step = (flags & DEMON_ODE_FINAL) != 0;
   const bool sde_curve = (flags & DEMON_ODE_SDE_CURVE) != 0, sde_bare = (flags & DEMON_ODE_SDE_BARE) != 0;
   const bool onc_on = (flags & DEMON_ODE_ONC) != 0;
+  const bool resc = (flags & DEMON_ODE_RESCALE) != 0;
+  const bool vs_on = (flags & DEMON_ODE_VS) != 0;
+  const bool x0t = (flags & DEMON_ODE_X0_TARGET) != 0;
+  const bool dec_out = (flags & DEMON_ODE_DEC_OUT) != 0, dec_mask = (flags & DEMON_ODE_DEC_MASK) != 0;
   const bool need_noise = !final_step && (sde_curve || (sde_bare && !mask) || (onc_on && !sde_bare));
+  const bool noise_in = need_noise && S.noise != nullptr;
+  const bool need_mask_data = mask || dec_mask;
   float kc[4], ac[4], sc[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -287,89 +333,123 @@ __global__ void __launch_bounds__(kOdeThreads) ode_step_kernel(const DemonOdeSlo
     sc[j] = cfg ? sh.sigma[c0 + j] : 0.f;
   }
 
-  for (int t = t0 + rg; t < t1; t += 16) {
-    const int64_t off = (int64_t)t * kOdeD + c0;
-    const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
-    float vt[4], x[4];
-    ld4(vp_s, loc, vt);
-    if (cfg) {
-      float r[4];
-      ld4(r_s, loc, r);
-      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
-      const bool resc = (flags & DEMON_ODE_RESCALE) != 0;
-      const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
+  for (int tb = t0 + rg; tb < t1; tb += 16 * kRB) {
+    uint2 ux[kRB], uor[kRB], unz[kRB], usrc[kRB], utg[kRB], ueps[kRB], ug[kRB];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float vg = vt[j] + w * (kc[j] * r[j] - ac[j] * vt[j]);
-        if (resc) vg = rho * (vg * sc[j]) + (1.0f - rho) * vg;
-        vt[j] = rnd(vg);
+    for (int i = 0; i < kRB; ++i) {
+      const int t = min(tb + 16 * i, t1 - 1);
+      const int64_t off = (int64_t)t * kOdeD + c0;
+      ux[i] = ldraw(S.xt, off);
+      if (need_mask_data) {
+        uor[i] = ldraw(S.mask_orig, off);
+        unz[i] = ldraw(S.mask_noise, off);
       }
+      if (sde_curve) usrc[i] = ldraw(S.source, off);
+      if (x0path && x0t) utg[i] = ldraw(S.x0_target, off);
+      if (noise_in) ueps[i] = ldraw(S.noise, off);
+      if (dec_out && gain) ug[i] = ldraw(gain, off);
     }
-    ld4(S.xt, off, x);
-    const float m = mask ? rnd(__ldg(S.mask + t) * S.mask_s) : 1.f;
-    if (mask) pre_blend(S, off, m, tc, x);
-    const float vs = (flags & DEMON_ODE_VS) ? rnd(curve(S.vscale, S.vscale_s, t)) : 1.f;
-    const float onc = onc_on ? rnd(curve(S.onc, S.onc_s, t)) : 0.f;
-    float eps[4] = {0.f, 0.f, 0.f, 0.f};
-    if (need_noise) {
-      if (S.noise) ld4(S.noise, off, eps);
-      else philox_normal4(S.seed, S.step, (uint64_t)off >> 2, eps);
-    }
-    float xn[4];
-    if (!x0path) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) xn[j] = x[j] + dt * (vt[j] * vs) + eps[j] * onc * tn;
-    } else {
-      float x0[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x0[j] = rnd(x[j] - rnd(rnd(vt[j] * vs) * tc));
-      if (mask) {
-        float o[4];
-        ld4(S.mask_orig, off, o);
-        const float om = rnd(1.0f - m);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x0[j] = rnd(rnd(m * x0[j]) + rnd(om * o[j]));
-      }
-      if (flags & DEMON_ODE_X0_TARGET) {
-        float tg[4];
-        ld4(S.x0_target, off, tg);
-        const float c = rnd(curve(S.x0_coef, S.x0_coef_s, t) * S.x0_coef_mul);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x0[j] = lerp_eager(x0[j], c, tg[j]);
-      }
-      if (sde_curve) {
-        float src[4];
-        ld4(S.source, off, src);
-        const float sdc = rnd(curve(S.sdc, S.sdc_s, t));
+    for (int i = 0; i < kRB; ++i) {
+      const int t = tb + 16 * i;
+      if (t >= t1) break;
+      const int64_t off = (int64_t)t * kOdeD + c0;
+      const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
+      float vt[4], x[4], o[4], nz[4];
+      ld4(vp_s, loc, vt);
+      if (cfg) {
+        float r[4];
+        ld4(r_s, loc, r);
+        const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
+        const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float full = tn * eps[j] + (1.0f - tn) * x0[j];
-          const float srcn = tn * eps[j] + (1.0f - tn) * src[j];
-          xn[j] = sdc * full + (1.0f - sdc) * srcn;
+          float vg = vt[j] + w * (kc[j] * r[j] - ac[j] * vt[j]);
+          if (resc) vg = rho * (vg * sc[j]) + (1.0f - rho) * vg;
+          vt[j] = rnd(vg);
         }
-      } else if (final_step) {
+      }
+      unpack4(ux[i], x);
+      if (need_mask_data) {
+        unpack4(uor[i], o);
+        unpack4(unz[i], nz);
+      }
+      const float m = mask ? rnd(__ldg(S.mask + t) * S.mask_s) : 1.f;
+      if (mask) {  // mask_pre_blend at t_curr (ode_steps.py:89-106), op by op
+        const float om = rnd(1.0f - m), ot = 1.0f - tc;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xn[j] = x0[j];
-      } else if (sde_bare) {
-        float nz[4];
-        if (mask) ld4(S.mask_noise, off, nz);
+        for (int j = 0; j < 4; ++j) x[j] = rnd(rnd(m * x[j]) + rnd(om * rnd(rnd(tc * nz[j]) + rnd(ot * o[j]))));
+      }
+      const float vs = vs_on ? rnd(curve(S.vscale, S.vscale_s, t)) : 1.f;
+      const float onc = onc_on ? rnd(curve(S.onc, S.onc_s, t)) : 0.f;
+      float eps[4] = {0.f, 0.f, 0.f, 0.f};
+      if (need_noise) {
+        if (noise_in) unpack4(ueps[i], eps);
+        else philox_normal4(S.seed, S.step, (uint64_t)off >> 2, eps);
+      }
+      float xn[4];
+      if (!x0path) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xn[j] = tn * (mask ? nz[j] : eps[j]) + (1.0f - tn) * x0[j];
+        for (int j = 0; j < 4; ++j) xn[j] = x[j] + dt * (vt[j] * vs) + eps[j] * onc * tn;
       } else {
+        float x0[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float vb = rnd(__fdiv_rn(rnd(x[j] - x0[j]), tc));
-          xn[j] = x[j] + dt * vb + eps[j] * onc * tn;
+        for (int j = 0; j < 4; ++j) x0[j] = rnd(x[j] - rnd(rnd(vt[j] * vs) * tc));
+        if (mask) {
+          const float om = rnd(1.0f - m);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) x0[j] = rnd(rnd(m * x0[j]) + rnd(om * o[j]));
+        }
+        if (x0t) {
+          float tg[4];
+          unpack4(utg[i], tg);
+          const float c = rnd(curve(S.x0_coef, S.x0_coef_s, t) * S.x0_coef_mul);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) x0[j] = lerp_eager(x0[j], c, tg[j]);
+        }
+        if (sde_curve) {
+          float src[4];
+          unpack4(usrc[i], src);
+          const float sdc = rnd(curve(S.sdc, S.sdc_s, t));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float full = tn * eps[j] + (1.0f - tn) * x0[j];
+            const float srcn = tn * eps[j] + (1.0f - tn) * src[j];
+            xn[j] = sdc * full + (1.0f - sdc) * srcn;
+          }
+        } else if (final_step) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xn[j] = x0[j];
+        } else if (sde_bare) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xn[j] = tn * (mask ? nz[j] : eps[j]) + (1.0f - tn) * x0[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float vb = rnd(__fdiv_rn(rnd(x[j] - x0[j]), tc));
+            xn[j] = x[j] + dt * vb + eps[j] * onc * tn;
+          }
         }
       }
-    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xn[j] = rnd(xn[j]);
-    st4(S.xt, off, xn);
-    if (flags & DEMON_ODE_DEC_OUT) {
-      const bool dm = (flags & DEMON_ODE_DEC_MASK) != 0;
-      const float mn = dm ? rnd(__ldg(S.mask + t) * S.mask_s_next) : 0.f;
-      write_dec(S, gain, off, t, dm, mn, tn, xn);
+      for (int j = 0; j < 4; ++j) xn[j] = rnd(xn[j]);
+      st4(S.xt, off, xn);
+      if (dec_out) {
+        float d[4] = {xn[0], xn[1], xn[2], xn[3]};
+        if (dec_mask) {  // mask_pre_blend at t_next with the next step's strength
+          const float mn = rnd(__ldg(S.mask + t) * S.mask_s_next);
+          const float om = rnd(1.0f - mn), ot = 1.0f - tn;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[j] = rnd(rnd(mn * d[j]) + rnd(om * rnd(rnd(tn * nz[j]) + rnd(ot * o[j]))));
+        }
+        if (gain) {
+          float gg[4];
+          unpack4(ug[i], gg);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[j] = d[j] * gg[j];
+        }
+        st4(S.dec_out, off, d);
+      }
     }
   }
 }
@@ -387,7 +467,7 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16);
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {
-    DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024));
     mark_device_done(attr_done);
   }
   cudaLaunchConfig_t cfg = {};

@@ -216,11 +216,12 @@ class NVFP4Linear(torch.nn.Module):
         self.packed = None
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-        """y = x W^T + b (+ hot LoRA), then optionally ``residual + gate * y``.
+                out: torch.Tensor | None = None, a: NVFP4Tensor | None = None) -> torch.Tensor:
+        """y = x W^T + b (+ hot LoRA), then optionally ``residual + bf16(y * gate)``.
 
         x: [..., K] bf16.  gate: [B, N] (one row per leading batch index, as the
         AdaLN gates of the DiT, turbo.py:525-546) or None.  residual: like the output.
+        a: ``quantize(x)`` when several linears share the input (q/k/v, gate/up).
         """
         if self.packed is None:
             self.repack()
@@ -228,7 +229,8 @@ class NVFP4Linear(torch.nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         if x2.stride(-1) != 1:
             x2 = x2.contiguous()
-        a = quantize(x2)
+        if a is None:
+            a = quantize(x2)
         lo = self.lora.active()
         xa = lb = None
         if lo is not None:
