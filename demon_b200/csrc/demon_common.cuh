@@ -131,6 +131,48 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// Same, with the source given as a shared-memory address.
+__device__ __forceinline__ void tma_store_2d_s(const void* tmap, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
+// Explicit shared-memory accesses by 32-bit address.  A pointer into dynamic shared
+// memory that went through integer arithmetic (alignment) loses its address space,
+// and generic loads/stores through it cost several times more than these.
+__device__ __forceinline__ void st_shared_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t a, float x) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(x) : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_f32x4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_global_v4(void* p, uint4 v) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// 64 contiguous bytes (32 bf16) of one row, as four 16-byte loads.
+__device__ __forceinline__ void ld_global_row64(const void* p, uint4 (&r)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    asm volatile("ld.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[j].x), "=r"(r[j].y), "=r"(r[j].z), "=r"(r[j].w)
+                 : "l"(reinterpret_cast<const uint8_t*>(p) + 16 * j));
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N bulk groups of this thread still read their shared-memory source.
 template <int N>

@@ -15,13 +15,14 @@
 //               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
 //               and commits to the stage's "empty" barrier.
 //   warps 2-9   epilogue, two warps per TMEM lane quadrant, each owning half of
-//               the tile's columns.  They drain their accumulator columns into
-//               registers with tcgen05.ld and release TMEM right away (the MMA
-//               warp starts the next tile while the epilogue computes
-//               alpha * acc + bias, gate * y, residual + y and stores), then
-//               stage 32x32 bf16 blocks in swizzled shared memory and write
-//               them with TMA stores.  A residual block is TMA-loaded into the
-//               same staging buffer and updated in place.
+//               the tile's columns.  Bias, row scales and L2 prefetches of the
+//               gate / residual rows are issued while the MMAs run; then the
+//               warps drain their accumulator columns into registers with
+//               tcgen05.ld and release TMEM at once (the MMA warp starts the
+//               next tile), convert each row to bf16 (alpha * acc + bias, one
+//               rounding), apply gate and residual in bf16 as the reference's
+//               eager ops do, and write 32x32 blocks through a double-buffered,
+//               64-byte-swizzled staging area with asynchronous TMA stores.
 // Hot LoRA: for each 64-wide slice of the rank, one extra pipeline stage holds
 // the xa tile (128 x 64 bf16, 16 KB -- the size of an A stage) and the
 // lora_b tile (BN x 64 bf16 -- the size of a B stage); four kind::f16 MMAs
@@ -63,8 +64,7 @@ constexpr int kBM = 128;
 constexpr int kRowBytes = 128;   // one 128-byte swizzle row per stage (256 fp4 / 64 bf16)
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kStgPitch = 80;     // staging row pitch: 32 bf16 + 16 bytes of padding (conflict-free)
-constexpr int kStageBuf = 32 * kStgPitch;
+constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
 template <int BN, int STAGES, bool FP4>
 struct GemmCfg {
@@ -76,9 +76,11 @@ struct GemmCfg {
   static constexpr int offB = offA + STAGES * kA;
   static constexpr int offSFA = offB + STAGES * kB;
   static constexpr int offSFB = offSFA + STAGES * kSFA;
+  // per epilogue warp: two 2 KB TMA-store staging buffers (FP4), or one transpose block (bf16)
+  static constexpr int kStgWarp = FP4 ? 4096 : 32 * kStgPitch;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
-  static constexpr int offBias = offStg + kEpiWarps * kStageBuf;
-  static constexpr int offBar = offBias + kEpiWarps * (BN / 2) * 2;
+  static constexpr int offCol = offStg + kEpiWarps * kStgWarp;  // fp32 per-column vector per warp
+  static constexpr int offBar = offCol + kEpiWarps * (BN / 2) * 4;
   static constexpr int kBars = 2 * STAGES + 3;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
@@ -110,7 +112,7 @@ template <int BN, int STAGES, bool FP4>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                const GemmParams p) {
+                const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
   using C = GemmCfg<BN, STAGES, FP4>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -271,22 +273,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;            // 0..7
     const int q = warp & 3;             // TMEM lane quadrant accessible to this warp
     const int half = ew >> 2;           // which half of the tile's columns
-    uint8_t* stg = smem + C::offStg + ew * kStageBuf;
-    __nv_bfloat16* bias_s = reinterpret_cast<__nv_bfloat16*>(smem + C::offBias) + ew * (BN / 2);
-    // transposed position of this lane: 8 rows x 4 granules of 16 bytes per pass
-    const int trow = lane >> 2, tgr = lane & 3;
-    uint32_t it = 0;
+    const uint32_t stg = smem_u32(smem + C::offStg + ew * C::kStgWarp);
+    const uint32_t colv = smem_u32(smem + C::offCol) + ew * (C::kColsPerWarp * 4);
+    if (FP4 && lane == 0) prefetch_tmap(&tmO);
+    uint32_t it = 0, nstore = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
       const int m0 = m_blk * kBM, n0 = n_blk * BN;
       const int ncol0 = n0 + half * C::kColsPerWarp;
-      // stage this warp's bias columns while the MMAs run
-      if (FP4) {
-        for (int i = lane; i < C::kColsPerWarp / 8; i += 32) {
-          uint4 bb = make_uint4(0u, 0u, 0u, 0u);
-          if (p.bias && ncol0 + i * 8 < p.N) bb = __ldg(reinterpret_cast<const uint4*>(p.bias + ncol0) + i);
-          reinterpret_cast<uint4*>(bias_s)[i] = bb;
-        }
+      // Everything that does not depend on the accumulator is fetched while the MMAs run:
+      // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
+      // the lane's row scale, and L2 prefetches of its gate / residual row segments.
+      for (int i = lane; i < C::kColsPerWarp; i += 32) {
+        const int n = ncol0 + i;
+        float cv = 0.0f;
+        if (n < p.N) cv = FP4 ? (p.bias ? __bfloat162float(p.bias[n]) : 0.0f) : p.col_scale[n];
+        st_shared_f32(colv + 4 * i, cv);
+      }
+      const int64_t row = (int64_t)m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const float alpha = row_ok ? p.a_gs[p.a_gs_per_row ? row : 0] * p.w_gs[0] : 0.0f;
+      const __nv_bfloat16* gate_row =
+          (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
+      const __nv_bfloat16* res_row = (FP4 && p.residual && row_ok) ? p.residual + row * p.ldr + ncol0 : nullptr;
+#pragma unroll
+      for (int j = 0; j < C::kColsPerWarp * 2; j += 128) {
+        if (gate_row) prefetch_l2(reinterpret_cast<const uint8_t*>(gate_row) + j);
+        if (res_row) prefetch_l2(reinterpret_cast<const uint8_t*>(res_row) + j);
       }
       __syncwarp();
       if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7)) break;
@@ -301,74 +314,98 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);  // TMEM drained: the next tile's MMAs may start
 
-      const int r_loc = q * 32 + lane;
-      const int64_t row = (int64_t)m0 + r_loc;
-      const bool row_ok = row < p.M;
-      const float ga = row_ok ? p.a_gs[p.a_gs_per_row ? row : 0] : 0.0f;
-      const float alpha = ga * p.w_gs[0];
+      // row domain, one row per lane: y = bf16(alpha * acc + bias), or bf16(acc * col_scale / alpha)
       const float inv_alpha = FP4 ? 0.0f : (row_ok ? 1.0f / alpha : 0.0f);
+      uint32_t y[C::kChunks][16];
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 cv = ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j));
+          if (FP4) {
+            y[c][2 * j] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][4 * j]), cv.x),
+                                      fmaf(alpha, __uint_as_float(v[c][4 * j + 1]), cv.y));
+            y[c][2 * j + 1] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][4 * j + 2]), cv.z),
+                                          fmaf(alpha, __uint_as_float(v[c][4 * j + 3]), cv.w));
+          } else {
+            y[c][2 * j] = pack_bf16x2(__uint_as_float(v[c][4 * j]) * (cv.x * inv_alpha),
+                                      __uint_as_float(v[c][4 * j + 1]) * (cv.y * inv_alpha));
+            y[c][2 * j + 1] = pack_bf16x2(__uint_as_float(v[c][4 * j + 2]) * (cv.z * inv_alpha),
+                                          __uint_as_float(v[c][4 * j + 3]) * (cv.w * inv_alpha));
+          }
+        }
+      }
+
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
         const int ncol = ncol0 + c * 32;
-        if (ncol >= p.N) break;  // uniform across the warp
-        // row domain: y = alpha * acc + bias (bf16), one row per lane
-        uint32_t w[16];
+        // FP4 tiles never cross N (N % BN == 0); the bf16 GEMM's last tile can (rank < BN)
+        if (!FP4 && ncol >= p.N) break;
         if (FP4) {
+          if (gate_row) {  // y = bf16(y * gate), as the reference's eager `y * gate`
+            uint4 gx[4];
+            ld_global_row64(gate_row + c * 32, gx);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 bb = reinterpret_cast<const uint4*>(bias_s + c * 32)[j];
-            const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t gw[4] = {gx[j].x, gx[j].y, gx[j].z, gx[j].w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              w[4 * j + i] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i]), bf16_lo(bw[i])),
-                                         fmaf(alpha, __uint_as_float(v[c][8 * j + 2 * i + 1]), bf16_hi(bw[i])));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n0c = ncol + 2 * i;
-            const float s0 = (n0c < p.N) ? p.col_scale[n0c] * inv_alpha : 0.0f;
-            const float s1 = (n0c + 1 < p.N) ? p.col_scale[n0c + 1] * inv_alpha : 0.0f;
-            w[i] = pack_bf16x2(__uint_as_float(v[c][2 * i]) * s0, __uint_as_float(v[c][2 * i + 1]) * s1);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(stg + lane * kStgPitch + j * 16) =
-              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        __syncwarp();
-        // transposed: lane covers rows trow + 8 s, columns ncol + 8 tgr .. +7
-#pragma unroll
-        for (int sp = 0; sp < 4; ++sp) {
-          const int rl = trow + 8 * sp;
-          const int64_t grow = (int64_t)m0 + q * 32 + rl;
-          uint4 o = *reinterpret_cast<const uint4*>(stg + rl * kStgPitch + tgr * 16);
-          const int cc = ncol + tgr * 8;
-          if (grow < p.M && cc < p.N) {
-            if (FP4 && (p.gate || p.residual)) {
-              uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-              if (p.gate) {  // y = bf16(y * gate), as the reference's eager `y * gate`
-                const uint4 gg = *reinterpret_cast<const uint4*>(p.gate + (grow / p.gate_rows) * p.ld_gate + cc);
-                const uint32_t gw[4] = {gg.x, gg.y, gg.z, gg.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  ow[i] = pack_bf16x2(bf16_lo(ow[i]) * bf16_lo(gw[i]), bf16_hi(ow[i]) * bf16_hi(gw[i]));
-              }
-              if (p.residual) {  // out = bf16(residual + y)
-                const uint4 rr = *reinterpret_cast<const uint4*>(p.residual + grow * p.ldr + cc);
-                const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  ow[i] = pack_bf16x2(bf16_lo(rw[i]) + bf16_lo(ow[i]), bf16_hi(rw[i]) + bf16_hi(ow[i]));
-              }
-              o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+              for (int i = 0; i < 4; ++i)
+                y[c][4 * j + i] = pack_bf16x2(bf16_lo(y[c][4 * j + i]) * bf16_lo(gw[i]),
+                                              bf16_hi(y[c][4 * j + i]) * bf16_hi(gw[i]));
             }
-            *reinterpret_cast<uint4*>(p.out + grow * p.ldo + cc) = o;
           }
+          if (res_row) {  // out = bf16(residual + y)
+            uint4 rx[4];
+            ld_global_row64(res_row + c * 32, rx);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                y[c][4 * j + i] = pack_bf16x2(bf16_lo(rw[i]) + bf16_lo(y[c][4 * j + i]),
+                                              bf16_hi(rw[i]) + bf16_hi(y[c][4 * j + i]));
+            }
+          }
+          // 32 rows x 32 columns, 64-byte swizzle (conflict-free), written by one TMA store;
+          // two buffers per warp: wait only until the store before last has read its source
+          const uint32_t buf = stg + (nstore & 1u) * 2048u;
+          if (nstore >= 2) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            st_shared_v4(buf + stg_off(lane, j), y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2], y[c][4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d_s(&tmO, buf, ncol, m0 + q * 32);  // rows >= M are clipped by the tensor map
+            bulk_commit();
+          }
+          ++nstore;
+        } else {
+          // bf16 GEMM (LoRA down-projection, narrow outputs): transpose through shared
+          // memory so each store instruction writes 8 rows x 64 contiguous bytes
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            st_shared_v4(stg + lane * kStgPitch + j * 16, y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2],
+                         y[c][4 * j + 3]);
+          __syncwarp();
+          const int trow = lane >> 2, tgr = lane & 3;
+#pragma unroll
+          for (int sp = 0; sp < 4; ++sp) {
+            const int rl = trow + 8 * sp;
+            const int64_t grow = (int64_t)m0 + q * 32 + rl;
+            const uint4 o = ld_shared_v4(stg + rl * kStgPitch + tgr * 16);
+            const int cc = ncol + tgr * 8;
+            if (grow < p.M && cc < p.N) st_global_v4(p.out + grow * p.ldo + cc, o);
+          }
+          __syncwarp();
         }
-        __syncwarp();
       }
     }
+    if (FP4 && lane == 0) bulk_wait_all();  // the staging buffers stay valid until every store has read them
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -381,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool FP4>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                GemmParams p, cudaStream_t st) {
+                const CUtensorMap& o, GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, FP4>;
   auto kern = gemm_kernel<BN, STAGES, FP4>;
   static std::atomic<uint64_t> attr_done{0};
@@ -396,7 +433,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   p.n_tiles = (p.N + BN - 1) / BN;
   const int tiles = p.m_tiles * p.n_tiles;
   const dim3 grid((unsigned)std::min(tiles, sms));
-  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, p);
+  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, o, p);
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
 }
@@ -447,6 +484,10 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                         (uint64_t)K / 2, 128, 128));
   DEMON_RC(make_tmap_2d(&tb, a->w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)N,
                         (uint64_t)K / 2, 128, BN));
+  // output: 32 x 32 bf16 store boxes (64-byte rows, 64-byte swizzle); rows past M are clipped
+  CUtensorMap to;
+  DEMON_RC(make_tmap_2d(&to, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                        (uint64_t)a->ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   if (lora) {
     const uint64_t r = (uint64_t)a->lora_rank;
     DEMON_RC(make_tmap_2d(&tla, a->lora_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)M, r * 2, 64, 128));
@@ -472,8 +513,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.a_gs_per_row = a->a_gs_per_row;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, p, st);
-  return launch_gemm<128, 5, true>(ta, tb, tla, tlb, p, st);
+  if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
+  return launch_gemm<128, 5, true>(ta, tb, tla, tlb, to, p, st);
 }
 
 extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* lora_a, int64_t rank,
@@ -506,9 +547,9 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   if (rank <= 64) {
     DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                           (uint64_t)K * 2, 64, 64));
-    return launch_gemm<64, 6, false>(ta, tb, tz, tz, p, st);
+    return launch_gemm<64, 6, false>(ta, tb, tz, tz, tz, p, st);
   }
   DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                         (uint64_t)K * 2, 64, 128));
-  return launch_gemm<128, 6, false>(ta, tb, tz, tz, p, st);
+  return launch_gemm<128, 6, false>(ta, tb, tz, tz, tz, p, st);
 }
