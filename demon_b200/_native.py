@@ -37,6 +37,7 @@ EXPORTED = (
     "demon_abi_version", "demon_struct_sizes", "demon_last_error", "demon_device_status",
     "demon_nvfp4_sf_bytes", "demon_nvfp4_quantize", "demon_nvfp4_gemm", "demon_lora_down",
     "demon_ode_step", "demon_ode_prepare", "demon_nvfp4_noalloc_scratch_bytes", "demon_nvfp4_linear_noalloc",
+    "demon_bf16_linear", "demon_adanorm_quantize", "demon_silu_mul_quantize", "demon_head_norm_rope",
 )
 
 _vp = ctypes.c_void_p
@@ -47,7 +48,7 @@ _f32 = ctypes.c_float
 
 class DemonGemmArgs(ctypes.Structure):
     _fields_ = [
-        ("a_codes", _vp), ("a_sf", _vp), ("a_gs", _vp), ("a_gs_per_row", _i32), ("_pad0", _i32),
+        ("a_codes", _vp), ("a_sf", _vp), ("a_gs", _vp), ("a_gs_per_row", _i32), ("w_gs_per_block", _i32),
         ("w_codes", _vp), ("w_sf", _vp), ("w_gs", _vp),
         ("M", _i64), ("N", _i64), ("K", _i64),
         ("out", _vp), ("ldo", _i64), ("bias", _vp), ("residual", _vp), ("ldr", _i64),
@@ -115,6 +116,11 @@ def load() -> ctypes.CDLL:
         L.demon_ode_step.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
         L.demon_ode_prepare.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
         L.demon_nvfp4_linear_noalloc.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp]
+        L.demon_bf16_linear.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp]
+        L.demon_adanorm_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp,
+                                             _vp, _i64, _vp]
+        L.demon_silu_mul_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]
+        L.demon_head_norm_rope.argtypes = [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _f32, _vp]
         for name in EXPORTED:
             getattr(L, name).restype = (_i64 if name in ("demon_nvfp4_sf_bytes", "demon_nvfp4_noalloc_scratch_bytes")
                                         else ctypes.c_int)

@@ -56,6 +56,7 @@ struct GemmParams {
   int64_t gate_rows, ld_gate, ldo, ldr;
   int M, N, K;
   int a_gs_per_row;
+  int w_gs_per_block;  // w_gs[n / 128] instead of w_gs[0]
   int lora_rank;
   int m_tiles, n_tiles;
 };
@@ -287,12 +288,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = lane; i < C::kColsPerWarp; i += 32) {
         const int n = ncol0 + i;
         float cv = 0.0f;
-        if (n < p.N) cv = FP4 ? (p.bias ? __bfloat162float(p.bias[n]) : 0.0f) : p.col_scale[n];
+        if (n < p.N)
+          cv = (FP4 || !p.col_scale) ? (p.bias ? __bfloat162float(p.bias[n]) : 0.0f) : p.col_scale[n];
         st_shared_f32(colv + 4 * i, cv);
       }
       const int64_t row = (int64_t)m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const float alpha = row_ok ? p.a_gs[p.a_gs_per_row ? row : 0] * p.w_gs[0] : 0.0f;
+      const float alpha = (row_ok && p.a_gs)
+                              ? p.a_gs[p.a_gs_per_row ? row : 0] * p.w_gs[p.w_gs_per_block ? ncol0 >> 7 : 0]
+                              : 0.0f;
       const __nv_bfloat16* gate_row =
           (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
       const __nv_bfloat16* res_row = (FP4 && p.residual && row_ok) ? p.residual + row * p.ldr + ncol0 : nullptr;
@@ -314,8 +318,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);  // TMEM drained: the next tile's MMAs may start
 
-      // row domain, one row per lane: y = bf16(alpha * acc + bias), or bf16(acc * col_scale / alpha)
-      const float inv_alpha = FP4 ? 0.0f : (row_ok ? 1.0f / alpha : 0.0f);
+      // row domain, one row per lane: y = bf16(alpha * acc + bias) (FP4), bf16(acc * col_scale / alpha)
+      // (LoRA down-projection) or bf16(acc + bias) (plain bf16 linear: no column scale)
+      const bool plain = !FP4 && !p.col_scale;
+      const float inv_alpha = (FP4 || plain) ? 0.0f : (row_ok ? 1.0f / alpha : 0.0f);
       uint32_t y[C::kChunks][16];
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
@@ -327,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       fmaf(alpha, __uint_as_float(v[c][4 * j + 1]), cv.y));
             y[c][2 * j + 1] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][4 * j + 2]), cv.z),
                                           fmaf(alpha, __uint_as_float(v[c][4 * j + 3]), cv.w));
+          } else if (plain) {
+            y[c][2 * j] = pack_bf16x2(__uint_as_float(v[c][4 * j]) + cv.x, __uint_as_float(v[c][4 * j + 1]) + cv.y);
+            y[c][2 * j + 1] =
+                pack_bf16x2(__uint_as_float(v[c][4 * j + 2]) + cv.z, __uint_as_float(v[c][4 * j + 3]) + cv.w);
           } else {
             y[c][2 * j] = pack_bf16x2(__uint_as_float(v[c][4 * j]) * (cv.x * inv_alpha),
                                       __uint_as_float(v[c][4 * j + 1]) * (cv.y * inv_alpha));
@@ -473,6 +483,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   DEMON_CHECK_ARG(!lora || (a->lora_b && a->lora_rank > 0 && a->lora_rank % 16 == 0 && a->lora_rank <= 128),
                   "gemm: LoRA needs lora_b and rank %% 16 == 0, 0 < rank <= 128 (rank=%lld)",
                   (long long)a->lora_rank);
+  DEMON_CHECK_ARG(!(lora && a->w_gs_per_block), "gemm: hot LoRA needs a single weight scale (w_gs_per_block = 0)");
   if (M == 0) return DEMON_OK;
 
   const bool bn256 = (N % 256 == 0);
@@ -511,6 +522,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.N = (int)N;
   p.K = (int)K;
   p.a_gs_per_row = a->a_gs_per_row;
+  p.w_gs_per_block = a->w_gs_per_block;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
@@ -551,5 +563,40 @@ extern "C" int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx,
   }
   DEMON_RC(make_tmap_2d(&tb, lora_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)rank,
                         (uint64_t)K * 2, 64, 128));
+  return launch_gemm<128, 6, false>(ta, tb, tz, tz, tz, p, st);
+}
+
+extern "C" int demon_bf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w, int64_t N,
+                                 const void* bias, void* out, int64_t ldo, void* stream) {
+  DEMON_API_BEGIN();
+  DEMON_CHECK_ARG(M >= 0 && K > 0 && K % 64 == 0 && N > 0 && N % 64 == 0,
+                  "bf16_linear: need K %% 64 == 0, N %% 64 == 0 (K=%lld N=%lld)", (long long)K, (long long)N);
+  DEMON_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "bf16_linear: dimension too large");
+  DEMON_CHECK_ARG(ldx >= K && ldx % 8 == 0 && ldo >= N && ldo % 8 == 0,
+                  "bf16_linear: ldx >= K, ldo >= N, both multiples of 8");
+  DEMON_CHECK_ARG(x && w && out, "bf16_linear: null pointer");
+  DEMON_CHECK_ARG(((uintptr_t)out & 15) == 0 && (!bias || ((uintptr_t)bias & 15) == 0),
+                  "bf16_linear: out and bias must be 16-byte aligned");
+  if (M == 0) return DEMON_OK;
+  CUtensorMap ta, tb, tz;
+  memset(&tz, 0, sizeof tz);
+  DEMON_RC(make_tmap_2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64,
+                        128));
+  GemmParams p{};
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.status = status_word();
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (N % 128 != 0) {
+    DEMON_RC(make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, 64,
+                          64));
+    return launch_gemm<64, 6, false>(ta, tb, tz, tz, tz, p, st);
+  }
+  DEMON_RC(make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, 64,
+                        128));
   return launch_gemm<128, 6, false>(ta, tb, tz, tz, tz, p, st);
 }

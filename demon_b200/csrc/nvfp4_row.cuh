@@ -1,0 +1,100 @@
+// nvfp4_row.cuh -- device helpers shared by the row kernels that end in NVFP4
+// quantisation (the activation quantiser and the fused DiT row kernels).
+// The arithmetic of each step is documented in nvfp4_quant.cu.
+#pragma once
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
+#include "demon_common.cuh"
+
+namespace demon {
+
+// E4M3FN byte -> float (format definition: bias 7, subnormals m * 2^-9).
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+  const uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+  const float v = (e == 0u) ? __int2float_rn((int)m) * 0.001953125f
+                            : __int2float_rn((int)(8u + m)) * __uint_as_float((e + 117u) << 23);  // 2^(e-10)
+  return (b & 0x80u) ? -v : v;
+}
+
+__device__ __forceinline__ uint32_t e4m3_rne_sat(float s) {
+  return (uint32_t)__nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ float global_scale(float amax) {
+  return __fdiv_rn(fmaxf(amax, 1e-12f), 2688.0f);
+}
+
+// Block absmax of 8 bf16 values with packed bf16x2 abs/max (exact: no rounding).
+__device__ __forceinline__ float amax8(uint4 v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+
+// Packed fp32 multiply (two IEEE round-to-nearest products per instruction).
+__device__ __forceinline__ float2 mul2(float2 a, float b) {
+  uint64_t r;
+  const uint64_t av = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
+  const uint64_t bv = (uint64_t)__float_as_uint(b) | ((uint64_t)__float_as_uint(b) << 32);
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(av), "l"(bv));
+  return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
+}
+
+// Two elements -> one byte of E2M1 codes (low nibble = first element) with
+// the hardware round-to-nearest-even, saturating conversion; NaN is mapped to
+// zero first (the format spec gives NaN code 0).
+__device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
+  lo = (lo == lo) ? lo : 0.0f;
+  hi = (hi == hi) ? hi : 0.0f;
+  return (uint32_t)__nv_cvt_float2_to_fp4x2(make_float2(lo, hi), __NV_E2M1, cudaRoundNearest);
+}
+
+// Eight elements -> 32 bits of codes.  A value that rounds to magnitude 0
+// keeps no sign bit (canonical zero, code 0).
+__device__ __forceinline__ uint32_t pack2(uint32_t w, float rs) {
+  const float2 p = mul2(make_float2(bf16_lo(w), bf16_hi(w)), rs);
+  return cvt2(p.x, p.y);
+}
+__device__ __forceinline__ uint32_t pack8(uint4 v, float rs) {
+  const uint32_t c = pack2(v.x, rs) | (pack2(v.y, rs) << 8) | (pack2(v.z, rs) << 16) | (pack2(v.w, rs) << 24);
+  const uint32_t mag = c & 0x77777777u;
+  const uint32_t nz = (mag | (mag >> 1) | (mag >> 2)) & 0x11111111u;
+  return mag | (c & (nz << 3));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One 8-element chunk of a row: block absmax (lanes 2i, 2i+1), scale, codes,
+// and the 32-bit scale-group store (lanes with lane % 8 == 0).  Every lane of
+// the warp calls this (the shuffles need the full warp); `valid` masks stores.
+__device__ __forceinline__ void quant_chunk(uint4 v, bool valid, int64_t c, int lane, float g, float denom,
+                                            uint32_t* code_row, uint8_t* sf_rowbase) {
+  const float mine = amax8(v);
+  const float am = fmaxf(mine, __shfl_xor_sync(0xffffffffu, mine, 1));
+  const float s = fminf(__fdiv_rn(am, denom), 448.0f);
+  const uint32_t sb = e4m3_rne_sat(s);
+  const float sbf = e4m3_value(sb);
+  uint32_t packed = 0u;
+  if (sbf != 0.0f) packed = pack8(v, __frcp_rn(__fmul_rn(sbf, g)));
+  const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 2);
+  const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 4);
+  const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 6);
+  if (valid) {
+    code_row[c] = packed;
+    if ((lane & 7) == 0)
+      *reinterpret_cast<uint32_t*>(sf_rowbase + ((c >> 1) >> 2) * 512) = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace demon

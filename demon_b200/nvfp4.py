@@ -29,7 +29,8 @@ class NVFP4Tensor:
     gs: torch.Tensor      # float32 [1] or [rows]
     rows: int
     K: int
-    per_row: bool = False  # gs holds one scale per row
+    per_row: bool = False    # gs holds one scale per row
+    per_block: bool = False  # weight: gs holds one scale per 128-row block (fused projections)
 
 
 def _check_cuda_bf16(x: torch.Tensor, name: str) -> None:
@@ -74,6 +75,43 @@ def pack_weight(w: torch.Tensor, stream=None) -> NVFP4Tensor:
     return quantize(w.contiguous(), nat.GS_DYNAMIC, stream=stream)
 
 
+def fuse_weights(parts: list) -> NVFP4Tensor:
+    """Concatenate packed weights that read the same activation (q/k/v, MLP gate/up) along N.
+
+    Codes and block scales concatenate as they are (every part has a multiple of 128 rows,
+    the scale layout's row block); each part keeps its own per-tensor global scale, given to
+    the GEMM as one scale per 128-column block of the fused output.
+    """
+    K = parts[0].K
+    for t in parts:
+        if t.K != K or t.rows % 128 or t.per_row or t.per_block or t.gs.numel() != 1:
+            raise ValueError("fuse_weights: parts need equal K, rows % 128 == 0 and one global scale each")
+    codes = torch.cat([t.codes for t in parts], 0)
+    sf = torch.cat([t.sf for t in parts], 0)
+    gs = torch.cat([t.gs.expand(t.rows // 128) for t in parts], 0).contiguous()
+    return NVFP4Tensor(codes, sf, gs, sum(t.rows for t in parts), K, per_block=True)
+
+
+def bf16_linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out = bf16(x @ w^T + bias) on the tensor cores, row by row independent of M.
+
+    x bf16 [M, K] (unit stride along K), w bf16 [N, K], bias bf16 [N] or None.
+    """
+    _check_cuda_bf16(x, "x")
+    _check_cuda_bf16(w, "w")
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("bf16_linear expects a 2-D x with unit stride along K")
+    M, K = x.shape
+    N = w.shape[0]
+    w = w.contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    nat.check(nat.load().demon_bf16_linear(nat.ptr(x), M, K, x.stride(0), nat.ptr(w), N, nat.ptr(bias),
+                                           nat.ptr(out), out.stride(0), nat.stream_ptr(stream)))
+    return out
+
+
 def lora_down(x: torch.Tensor, lora_a: torch.Tensor, col_scale: torch.Tensor, a: NVFP4Tensor,
               w: NVFP4Tensor, stream=None) -> torch.Tensor:
     """xa = col_scale * (x @ lora_a^T) / (a_gs * w_gs), bf16 [M, r] (tcgen05 bf16 GEMM)."""
@@ -102,6 +140,7 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
     args = nat.DemonGemmArgs()
     args.a_codes, args.a_sf, args.a_gs = nat.ptr(a.codes), nat.ptr(a.sf), nat.ptr(a.gs)
     args.a_gs_per_row = int(a.per_row)
+    args.w_gs_per_block = int(w.per_block)
     args.w_codes, args.w_sf, args.w_gs = nat.ptr(w.codes), nat.ptr(w.sf), nat.ptr(w.gs)
     args.M, args.N, args.K = M, N, K
     args.out, args.ldo = nat.ptr(out), out.stride(0)

@@ -81,7 +81,7 @@ DEMON_API int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t 
 /*
  * Block-scaled NVFP4 GEMM with fused epilogue:
  *   acc[m,n] = sum_k a[m,k] * w[n,k]                        (tcgen05, fp32 in TMEM)
- *   y[m,n]   = alpha_m * (acc[m,n] + lora[m,n]) + bias[n]   alpha_m = a_gs[m|0] * w_gs[0]
+ *   y[m,n]   = alpha * (acc[m,n] + lora[m,n]) + bias[n]     alpha = a_gs[m|0] * w_gs[0 | n/128]
  *   lora     = sum_j lora_xa[m,j] * lora_b[n,j]             (tcgen05 bf16 MMA into the same
  *                                                            accumulator; lora_xa comes from
  *                                                            demon_lora_down, already divided
@@ -93,17 +93,20 @@ DEMON_API int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t 
  * 286-289, 311-345, 377, 538) plus the gated residual that follows o_proj / MLP
  * (turbo.py:525-546), and for the LoRA writeback W = base + sum s_i B_i A_i
  * (acestep/engine/lora.py:283-366, 811-833) without rewriting W.
- * Constraints: K % 256 == 0, N % 32 == 0, ldo/ldr % 8 == 0, lora_rank % 16 == 0 and <= 128.
+ * w_gs_per_block: w_gs holds N/128 scales, one per 128-column block, so that several
+ * linears that read the same activation (q/k/v, MLP gate/up) run as one GEMM over their
+ * concatenated packed weights while each keeps its own per-tensor scale.
+ * Constraints: K % 256 == 0, N % 128 == 0, ldo/ldr % 8 == 0, lora_rank % 16 == 0 and <= 128.
  */
 typedef struct DemonGemmArgs {
   const uint8_t* a_codes; /* [M, K/2] */
   const uint8_t* a_sf;    /* demon_nvfp4_sf_bytes(M, K) */
   const float* a_gs;      /* [1] or [M] */
   int32_t a_gs_per_row;
-  int32_t _pad0;
+  int32_t w_gs_per_block;
   const uint8_t* w_codes; /* [N, K/2] */
   const uint8_t* w_sf;    /* demon_nvfp4_sf_bytes(N, K) */
-  const float* w_gs;      /* [1] */
+  const float* w_gs;      /* [1], or [N/128] with w_gs_per_block */
   int64_t M, N, K;
   void* out;              /* bf16 [M, ldo] */
   int64_t ldo;
@@ -130,6 +133,51 @@ DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);
 DEMON_API int demon_lora_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* lora_a, int64_t rank,
                     const float* col_scale, const float* a_gs, int a_gs_per_row, const float* w_gs, void* xa,
                     void* stream);
+
+/*
+ * bf16 linear on the tensor cores (tcgen05 kind::f16, fp32 accumulate, one rounding):
+ *   out[m, n] = bf16(sum_k x[m,k] * w[n,k] + bias[n])
+ * x bf16 [M, ldx], w bf16 [N, K] (nn.Linear layout), bias bf16 [N] or NULL, out bf16 [M, ldo].
+ * For the DiT projections the reference keeps in bf16: proj_in (Conv1d, kernel = stride =
+ * patch, as a linear over patches), proj_out (ConvTranspose1d likewise) and the timestep
+ * embedding MLPs (acestep/models/modeling_acestep_v15_turbo.py:207-261, 1262-1307).  Every
+ * output row depends on its own input row only (fixed tile shape and summation order), so a
+ * slot's result does not depend on the batch it is computed in.
+ * K % 64 == 0, N % 64 == 0, ldx/ldo % 8 == 0.
+ */
+DEMON_API int demon_bf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx, const void* w, int64_t N,
+                                const void* bias, void* out, int64_t ldo, void* stream);
+
+/*
+ * DiT row kernels around the NVFP4 GEMMs.  Every output row is computed by a fixed set of
+ * lanes in a fixed order, independent of M, so results do not depend on the batch.
+ *
+ * demon_adanorm_quantize: per row of x bf16 [M, D]
+ *   y = bf16(bf16(bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps))) * scale1[b]) + shift[b]),
+ *   b = m / rows_per_mod, scale1 = 1 + scale (bf16 [B, ld_mod]; NULL skips the product,
+ *   shift NULL skips the sum), then NVFP4-quantised with a per-row global scale into
+ *   codes / sf / gs (NULL codes: no quantisation) and/or stored as bf16 into y [M, ldy].
+ *   Stands in for Qwen3RMSNorm + the AdaLN modulation of AceStepDiTLayer.forward and the
+ *   output norm of AceStepDiTModel.forward (acestep/models/modeling_acestep_v15_turbo.py:
+ *   508-510, 522, 531-538, 1495-1500) followed by the activation quantiser.
+ *   D in {256, 512, 1024, 2048, 3072, 4096, 6144, 8192}.
+ * demon_silu_mul_quantize: gu bf16 [M, ld] holds gate in columns [0, F) and up in [F, 2F);
+ *   h = bf16(bf16(silu(gate)) * up), NVFP4-quantised per row (Qwen3MLP's act_fn(gate) * up,
+ *   turbo.py:34-35).  F as D above.
+ * demon_head_norm_rope: in place on `heads` heads of 128 columns starting at col0 of
+ *   x bf16 [M, ld]: Qwen3RMSNorm over each head (weight w [128]), then, when cos/sin
+ *   (bf16 [S, 128], position = m % S) are given, x * cos + rotate_half(x) * sin with each
+ *   product and the sum rounded to bf16 (q_norm / k_norm and apply_rotary_pos_emb in
+ *   AceStepAttention.forward, turbo.py:311-345).
+ */
+DEMON_API int demon_adanorm_quantize(const void* x, int64_t M, int64_t D, int64_t ldx, const void* norm_w,
+                                     const void* scale1, const void* shift, int64_t rows_per_mod, int64_t ld_mod,
+                                     float eps, float* gs, uint8_t* codes, uint8_t* sf, void* y, int64_t ldy,
+                                     void* stream);
+DEMON_API int demon_silu_mul_quantize(const void* gu, int64_t M, int64_t F, int64_t ld, float* gs, uint8_t* codes,
+                                      uint8_t* sf, void* stream);
+DEMON_API int demon_head_norm_rope(void* x, int64_t M, int64_t ld, int64_t col0, int64_t heads, const void* w,
+                                   const void* cos, const void* sin, int64_t S, float eps, void* stream);
 
 /*
  * NVFP4 linear that allocates nothing: out = x W^T + bias (bf16 [M, ldo]),
