@@ -104,9 +104,15 @@ class TimestepEmbedding(nn.Module):
         self.time_proj = nn.Linear(dim, dim * 6)
         self.scale = scale
 
+    def _freqs(self, device):
+        cache = self.__dict__.setdefault("_freq_cache", {})
+        if device not in cache:  # computed on the CPU as the reference does, then kept on the device
+            half = self.in_channels // 2
+            cache[device] = torch.exp(-math.log(10000) * torch.arange(0, half, dtype=torch.float32) / half).to(device)
+        return cache[device]
+
     def forward(self, t):
-        half = self.in_channels // 2
-        freqs = torch.exp(-math.log(10000) * torch.arange(0, half, dtype=torch.float32) / half).to(t.device)
+        freqs = self._freqs(t.device)
         args = (t * self.scale)[:, None].float() * freqs[None]
         emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1).to(t.dtype)
         temb = Q.bf16_linear(torch.nn.functional.silu(Q.bf16_linear(emb, self.linear_1.weight, self.linear_1.bias)),
@@ -311,6 +317,7 @@ class DemonDiT(nn.Module):
     def _load_from_state_dict(self, *args, **kwargs):
         super()._load_from_state_dict(*args, **kwargs)
         self._conv_cache = None
+        Q.bump_generation()
 
     def _rope(self, S, device, dtype):
         key = (S, device, dtype)
@@ -357,6 +364,7 @@ class DemonDiT(nn.Module):
             if isinstance(m, (Attention, MLP)):
                 m._fused = None
         self._conv_cache = None
+        Q.bump_generation()
         return self
 
     def encoder_kv(self, encoder_hidden_states):

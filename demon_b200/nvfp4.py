@@ -21,6 +21,19 @@ import torch
 from . import _native as nat
 
 
+# Bumped whenever a packed weight or a hot-LoRA bank changes; captured CUDA graphs that
+# bake in weight / LoRA pointers compare it before replaying.
+_GENERATION = [0]
+
+
+def weights_generation() -> int:
+    return _GENERATION[0]
+
+
+def bump_generation() -> None:
+    _GENERATION[0] += 1
+
+
 @dataclass
 class NVFP4Tensor:
     """Packed NVFP4 operand: E2M1 codes, tcgen05-layout E4M3 block scales, fp32 global scale(s)."""
@@ -180,18 +193,22 @@ class LoRABank:
         self.entries[lora_id] = _LoRAEntry(A.to(torch.bfloat16).contiguous(), B.to(torch.bfloat16).contiguous(),
                                            float(strength))
         self._cat = None
+        bump_generation()
 
     def remove(self, lora_id: str) -> None:
         self.entries.pop(lora_id, None)
         self._cat = None
+        bump_generation()
 
     def set_strength(self, lora_id: str, strength: float) -> None:
         self.entries[lora_id].strength = float(strength)
         self._cat = None
+        bump_generation()
 
     def enable(self, lora_id: str, enabled: bool = True) -> None:
         self.entries[lora_id].enabled = enabled
         self._cat = None
+        bump_generation()
 
     def active(self):
         """(A_cat [R, K], B_cat [N, R], col_scale fp32 [R]) or None when no LoRA contributes."""
@@ -246,6 +263,7 @@ class NVFP4Linear(torch.nn.Module):
         return m
 
     def repack(self) -> None:
+        bump_generation()
         self.packed = pack_weight(self.weight.data)
         if not self.keep_weight:
             self.weight.data = torch.empty(0, dtype=torch.bfloat16, device=self.weight.device)
@@ -253,6 +271,7 @@ class NVFP4Linear(torch.nn.Module):
     def _load_from_state_dict(self, *args, **kwargs):
         super()._load_from_state_dict(*args, **kwargs)
         self.packed = None
+        bump_generation()
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, a: NVFP4Tensor | None = None) -> torch.Tensor:

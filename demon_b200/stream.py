@@ -27,6 +27,7 @@ from typing import Callable, List, Optional, Tuple
 
 import torch
 
+from . import nvfp4 as Q
 from . import ode as O
 
 
@@ -109,6 +110,60 @@ class SlotRequest:
         return True
 
 
+class GraphedDecoder:
+    """Replays the decoder forward as one CUDA graph per input shape.
+
+    A DiT forward is ~400 kernel launches; replaying a captured graph removes the host
+    launch cost between them.  Inputs are copied into the graph's static buffers before
+    each replay; graphs are dropped when any packed weight or hot-LoRA bank changed
+    (``nvfp4.weights_generation``), since they bake in those device pointers.
+    """
+
+    def __init__(self, decoder):
+        self.decoder = decoder
+        self._graphs: dict = {}
+        self._gen = None
+        self._pool = None
+
+    def _capture(self, x, t, enc, ctx):
+        static = [x.clone(), t.clone(), enc.clone(), ctx.clone()]
+
+        def run():
+            return self.decoder(hidden_states=static[0], timestep=static[1], timestep_r=static[1],
+                                attention_mask=None, encoder_hidden_states=static[2],
+                                encoder_attention_mask=None, context_latents=static[3], use_cache=False,
+                                past_key_values=None)[0]
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            run()  # warm-up: packs weights, sets kernel attributes, fills caches
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._pool):
+            out = run()
+        return g, static, out
+
+    def __call__(self, hidden_states, timestep, timestep_r=None, attention_mask=None, encoder_hidden_states=None,
+                 encoder_attention_mask=None, context_latents=None, use_cache=False, past_key_values=None, **kw):
+        gen = Q.weights_generation()
+        if gen != self._gen:
+            self._graphs.clear()
+        key = (tuple(hidden_states.shape), tuple(encoder_hidden_states.shape), tuple(context_latents.shape))
+        ent = self._graphs.get(key)
+        if ent is None:
+            ent = self._capture(hidden_states, timestep, encoder_hidden_states, context_latents)
+            self._graphs[key] = ent
+            self._gen = Q.weights_generation()
+        g, static, out = ent
+        for dst, src in zip(static, (hidden_states, timestep, encoder_hidden_states, context_latents)):
+            dst.copy_(src)
+        g.replay()
+        # a copy: the next replay of the same shape (e.g. the negative pass) reuses `out`
+        return out.clone(), past_key_values
+
+
 @dataclass
 class StreamConfig:
     """The DiffusionConfig fields the tick reads (acestep/engine/diffusion.py:13-59).
@@ -151,8 +206,8 @@ class StreamPipeline:
     fused ODE launch per tick."""
 
     def __init__(self, decoder, config: Optional[StreamConfig] = None, pipeline_depth: Optional[int] = None,
-                 device=None, dtype=torch.bfloat16):
-        self.decoder = decoder
+                 device=None, dtype=torch.bfloat16, use_graphs: bool = False):
+        self.decoder = GraphedDecoder(decoder) if use_graphs else decoder
         self.config = config or StreamConfig()
         self._depth = pipeline_depth if pipeline_depth is not None else self.config.infer_steps
         self._slots: List[Optional[_Slot]] = [None] * self._depth

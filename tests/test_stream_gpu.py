@@ -68,12 +68,9 @@ def _requests(dev):
     return reqs
 
 
-def test_stream_equals_batch(cuda):
-    from demon_b200.stream import StreamConfig, StreamPipeline, generate
-    dec = _decoder(cuda)
-    cfg = StreamConfig(infer_steps=8)
-    reqs = _requests(cuda)
-    pipe = StreamPipeline(dec, cfg, pipeline_depth=4, device=cuda)
+def _run_stream(dec, cfg, reqs, dev, **kw):
+    from demon_b200.stream import StreamPipeline
+    pipe = StreamPipeline(dec, cfg, pipeline_depth=4, device=dev, **kw)
     outs = []
     pending = list(reqs)
     for _ in range(200):
@@ -86,6 +83,15 @@ def test_stream_equals_batch(cuda):
             break
     assert len(outs) == len(reqs)
     assert pipe.stats()["ticks"] > 8
+    return outs
+
+
+def test_stream_equals_batch(cuda):
+    from demon_b200.stream import StreamConfig, generate
+    dec = _decoder(cuda)
+    cfg = StreamConfig(infer_steps=8)
+    reqs = _requests(cuda)
+    outs = _run_stream(dec, cfg, reqs, cuda)
     for i, req in enumerate(reqs):
         alone = generate(dec, req, cfg, device=cuda)
         assert alone.shape == (1, T, 64)
@@ -93,3 +99,14 @@ def test_stream_equals_batch(cuda):
         assert torch.equal(outs[i], alone), f"request {i}: stream and batch paths differ"
     # the requests really are different computations
     assert not torch.equal(outs[0], outs[1])
+
+
+def test_stream_graph_replay_equals_eager(cuda):
+    """The CUDA-graph decoder (one graph per batch shape) gives the eager path's bits."""
+    from demon_b200.stream import StreamConfig
+    dec = _decoder(cuda)
+    cfg = StreamConfig(infer_steps=8)
+    eager = _run_stream(dec, cfg, _requests(cuda), cuda)
+    graphed = _run_stream(dec, cfg, _requests(cuda), cuda, use_graphs=True)
+    for i, (a, b) in enumerate(zip(eager, graphed)):
+        assert torch.equal(a, b), i
