@@ -344,20 +344,24 @@ class DemonDiT(nn.Module):
     @torch.no_grad()
     def init_random_(self, seed: int = 0) -> "DemonDiT":
         """Seeded random weights (there are no checkpoints offline): N(0, 1/fan_in) linears and
-        convolutions, norms 1, AdaLN tables N(0, 1/D), biases 0."""
-        g = torch.Generator().manual_seed(seed)
+        convolutions, norms 1, AdaLN tables N(0, 1/D), biases 0.  Drawn on the parameters'
+        device (same seed and device type -> same weights)."""
+        dev = next(self.parameters()).device
+        g = torch.Generator(device=dev).manual_seed(seed)
         for name, p in self.named_parameters():
             shape = p.shape
             if name.endswith("norm.weight") or name.endswith("norm_out.weight"):
-                v = torch.ones(shape)
-            elif name.endswith("scale_shift_table"):
-                v = torch.randn(shape, generator=g) / shape[-1] ** 0.5
-            elif name.endswith(".bias"):
-                v = torch.zeros(shape)
+                p.data.fill_(1.0)
+                continue
+            if name.endswith(".bias"):
+                p.data.zero_()
+                continue
+            if name.endswith("scale_shift_table"):
+                std = 1.0 / shape[-1] ** 0.5
             else:
                 fan_in = shape[0] if "proj_out" in name else shape[1] * (shape[2] if len(shape) > 2 else 1)
-                v = torch.randn(shape, generator=g) / fan_in ** 0.5
-            p.data.copy_(v.to(p.dtype))
+                std = 1.0 / fan_in ** 0.5
+            p.data.copy_((torch.randn(shape, generator=g, device=dev) * std).to(p.dtype))
         for m in self.modules():
             if isinstance(m, NVFP4Linear):
                 m.packed = None

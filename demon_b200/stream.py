@@ -199,6 +199,9 @@ class _Slot:
     neg_cache: Optional[torch.Tensor] = None
     neg_cached_valid: bool = False
     mask: Optional[O.LatentMask] = None
+    conds: list = field(default_factory=list)   # request.all_conditions(), built once
+    ctx: Optional[torch.Tensor] = None          # context latents on the device
+    enc: dict = field(default_factory=dict)     # id(condition) -> encoder states on the device
 
 
 class StreamPipeline:
@@ -361,6 +364,11 @@ class StreamPipeline:
             sl.initial_noise = noise.clone()
         if req.rcfg_mode == "initialize":
             sl.neg_cache = torch.zeros(T, D, dtype=self._dtype, device=self._device)
+        # the request's conditioning moves to the device once (host requests: one H2D per slot)
+        sl.ctx = req.context_latents.to(self._device, self._dtype, non_blocking=True)
+        sl.conds = req.all_conditions()
+        for c in sl.conds + list(req.neg_conditions):
+            sl.enc[id(c)] = c.encoder_hidden_states.to(self._device, self._dtype, non_blocking=True)
         if req.latent_mask is not None:
             lm = req.latent_mask
             if lm.noise is None:
@@ -372,7 +380,7 @@ class StreamPipeline:
 
     def _active_conds(self, sl: _Slot):
         total = len(sl.t_schedule) - 1
-        conds = sl.request.all_conditions()
+        conds = sl.conds
         act = [c for c in conds if c.is_active_at_step(sl.step_idx, total)]
         return act if act else [conds[0]]
 
@@ -390,13 +398,13 @@ class StreamPipeline:
         xb = self._dec.index_select(0, idx)
         mL = max(c.encoder_hidden_states.shape[1] for _, c in rows)
         enc = []
-        for _, c in rows:
-            e = c.encoder_hidden_states.to(self._device, self._dtype)
-            if e.shape[1] < mL:
+        for si, c in rows:
+            e = slots[si].enc[id(c)]
+            if e.shape[1] < mL:  # zero padding to the longest condition, as the reference does
                 e = torch.nn.functional.pad(e, (0, 0, 0, mL - e.shape[1]))
             enc.append(e)
         enc = torch.cat(enc, 0)
-        ctx = torch.cat([slots[si].request.context_latents.to(self._device, self._dtype) for si, _ in rows], 0)
+        ctx = torch.cat([slots[si].ctx for si, _ in rows], 0)
         t = torch.tensor([float(slots[si].t_schedule[slots[si].step_idx]) for si, _ in rows],
                          device=self._device, dtype=self._dtype)
         out = self.decoder(hidden_states=xb, timestep=t, timestep_r=t, attention_mask=None,
@@ -437,7 +445,19 @@ class StreamPipeline:
 
     @torch.no_grad()
     def tick(self) -> Optional[torch.Tensor]:
-        """stream.py:849-917 with the post-forward section as one fused launch."""
+        """stream.py:849-917 with the post-forward section as one fused launch: returns the
+        finished latent [1, T, 64] of at most one slot, like the reference."""
+        out = self._tick(pop_all=False)
+        return out[0] if out else None
+
+    @torch.no_grad()
+    def tick_many(self) -> List[torch.Tensor]:
+        """One tick that pops every finished slot (the reference pops one per tick, which
+        stalls rings deeper than the step count): a ring of depth > infer_steps then keeps
+        every slot active.  Returns the finished latents [1, T, 64] in slot order."""
+        return self._tick(pop_all=True)
+
+    def _tick(self, pop_all: bool) -> List[torch.Tensor]:
         t_start = time.time()
         if self._queue:
             target_T = self._queue[-1].context_latents.shape[1]
@@ -445,12 +465,13 @@ class StreamPipeline:
             for i, s in enumerate(self._slots):
                 if s is not None and s.xt.shape[0] != target_T:
                     self._slots[i] = None
-        finished = None
+        finished = []
         for i, s in enumerate(self._slots):
             if s is not None and s.step_idx >= len(s.t_schedule) - 1:
-                finished = s.xt.unsqueeze(0)
+                finished.append(s.xt.unsqueeze(0))
                 self._slots[i] = None
-                break
+                if not pop_all:
+                    break
         new = []
         for i, s in enumerate(self._slots):
             if s is None and self._queue:

@@ -1,0 +1,91 @@
+"""The slot-sharded ring's collective plumbing on two CPU ranks (gloo).
+
+The ring's compute (StreamPipeline on a GPU) is replaced by a fake pipeline that finishes
+deterministic latents and records shared-curve updates, so the test covers exactly the
+multi-process part: slot ownership, curve broadcast tagged with the tick (applied on every
+rank at tag + 1) and the gather of finished latents to rank 0 in rank order.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+T = 16
+
+
+class FakePipe:
+    def __init__(self, rank):
+        self.rank, self.t = rank, 0
+        self.curves = []          # (tick, name, first value or None)
+
+    def set_shared_curve(self, name, v):
+        self.curves.append((self.t, name, None if v is None else float(v[0])))
+
+    def tick_many(self):
+        out = []
+        if self.t % 2 == self.rank:   # each rank finishes one latent every other tick
+            out.append(torch.full((1, T, 64), float(100 * self.rank + self.t)).to(torch.bfloat16))
+        self.t += 1
+        return out
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from demon_b200.ring import ShardedRing
+    pipe = FakePipe(rank)
+    ring = ShardedRing(pipe, rank, world, T, "cpu", curve_names=["velocity_scale", "guidance_curve"],
+                       curve_every=4, max_finished=2)
+
+    def src(tick):
+        return {"velocity_scale": torch.full((T,), 1.0 + tick), "guidance_curve": None if tick % 8 else
+                torch.full((T,), 3.0 + tick)}
+    gathered = []
+    for _ in range(10):
+        _, g = ring.step(src)
+        if g is not None:
+            gathered.append([float(x[0, 0, 0]) for x in g])
+    q.put((rank, [ring.owns(i) for i in range(8)], pipe.curves, gathered))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_sharded_ring_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, owns, curves, gathered = q.get(timeout=120)
+        res[r] = (owns, curves, gathered)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # ownership: global slot g on rank g % 2
+    assert res[0][0] == [g % 2 == 0 for g in range(8)]
+    assert res[1][0] == [g % 2 == 1 for g in range(8)]
+    # curves broadcast at ticks 0, 4, 8 apply at ticks 1, 5, 9 on both ranks, identically
+    assert res[0][1] == res[1][1]
+    applied = {(t, n): v for t, n, v in res[0][1]}
+    assert applied[(1, "velocity_scale")] == 1.0 and applied[(1, "guidance_curve")] == 3.0
+    assert applied[(5, "velocity_scale")] == 5.0 and applied[(5, "guidance_curve")] is None
+    assert applied[(9, "velocity_scale")] == 9.0 and applied[(9, "guidance_curve")] == 11.0
+    assert sorted({t for t, _, _ in res[0][1]}) == [1, 5, 9]
+    # rank 0 gathers every finished latent, rank 0's first: tick t finishes on rank t % 2
+    assert res[1][2] == []
+    assert res[0][2] == [[100.0 * (t % 2) + t] for t in range(10)]
