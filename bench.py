@@ -335,7 +335,7 @@ def measure_quantize_big(dev, stream, M=12000, K=2048, reps=10):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
     nbytes = M * K * 2 + M * K // 2 + M * K // 16 + M * 4
-    return {"kernel": "demon::quantize_rows_kernel<2,2>", "workload": f"x bf16 [{M}, {K}], per-row scales",
+    return {"kernel": "demon::quantize_blocks_kernel<2,2048>", "workload": f"x bf16 [{M}, {K}], per-row scales",
             "us": us, "bytes": nbytes, "achieved": nbytes / (us * 1e-6) / 1e9, "unit": "GB/s"}
 
 

@@ -54,6 +54,8 @@ class DemonGemmArgs(ctypes.Structure):
         ("out", _vp), ("ldo", _i64), ("bias", _vp), ("residual", _vp), ("ldr", _i64),
         ("gate", _vp), ("gate_rows", _i64), ("ld_gate", _i64),
         ("lora_xa", _vp), ("lora_b", _vp), ("lora_rank", _i64),
+        ("hn_cols", _i64), ("hn_q_cols", _i64), ("rope_S", _i64), ("hn_wq", _vp), ("hn_wk", _vp),
+        ("rope_cos", _vp), ("rope_sin", _vp), ("hn_eps", _f32), ("_pad1", _i32),
     ]
 
 

@@ -24,30 +24,6 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) { return pack_bf16x2(lo, hi); }
 
-// Row-block geometry shared by the fused row kernels: a row of D = W * 256 * NCH elements is
-// held by W warps; lane l of row-warp w owns the 8-element chunks c = w*32*NCH + 32 j + l, so
-// lanes (2i, 2i+1) own one 16-element scale block, as in the activation quantiser.
-template <int W, int NCH>
-struct RowGeo {
-  static constexpr int kRowsPerCta = 8 / W;
-  static constexpr int kD = W * 256 * NCH;
-};
-
-// Cross-warp reduction of one value per row (sum or max) through shared memory.
-template <int W, bool MAX>
-__device__ __forceinline__ float row_reduce(float v, float* red, int warp, int lane) {
-  v = MAX ? warp_max(v) : warp_sum(v);
-  if (W == 1) return v;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  const int w0 = warp - warp % W;
-  float r = red[w0];
-#pragma unroll
-  for (int i = 1; i < W; ++i) r = MAX ? fmaxf(r, red[w0 + i]) : r + red[w0 + i];
-  return r;
-}
-
 struct NormArgs {
   const __nv_bfloat16* x;
   int64_t M, ldx, Mpad;
@@ -63,95 +39,111 @@ struct NormArgs {
   int64_t ldy;
 };
 
+// Eight bf16 (x) -> bf16(bf16(bf16(w * bf16(x * rinv)) * s1) + sh) (products / sum skipped
+// when s1 / sh are absent), as Qwen3RMSNorm followed by the AdaLN modulation.
+template <bool MUL, bool ADD>
+__device__ __forceinline__ uint4 norm8(uint4 x, uint4 w, uint4 s1, uint4 sh, float rinv) {
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, ww[4] = {w.x, w.y, w.z, w.w};
+  const uint32_t sw[4] = {s1.x, s1.y, s1.z, s1.w}, hw[4] = {sh.x, sh.y, sh.z, sh.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lo = bf16r(__fmul_rn(bf16_lo(ww[i]), bf16r(__fmul_rn(bf16_lo(xw[i]), rinv))));
+    float hi = bf16r(__fmul_rn(bf16_hi(ww[i]), bf16r(__fmul_rn(bf16_hi(xw[i]), rinv))));
+    if (MUL) {
+      lo = bf16r(__fmul_rn(lo, bf16_lo(sw[i])));
+      hi = bf16r(__fmul_rn(hi, bf16_hi(sw[i])));
+    }
+    if (ADD) {
+      lo = bf16r(__fadd_rn(lo, bf16_lo(hw[i])));
+      hi = bf16r(__fadd_rn(hi, bf16_hi(hw[i])));
+    }
+    o[i] = pack_bf16(lo, hi);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ float sumsq8(uint4 v, float acc) {
+  const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc = __fadd_rn(acc, __fmul_rn(bf16_lo(w4[i]), bf16_lo(w4[i])));
+    acc = __fadd_rn(acc, __fmul_rn(bf16_hi(w4[i]), bf16_hi(w4[i])));
+  }
+  return acc;
+}
+
 // y = ((w * bf16(x * rsqrt(mean(x^2) + eps))) * (1 + scale)) + shift, each product / sum
 // rounded to bf16 as Qwen3RMSNorm and the AdaLN lines of AceStepDiTLayer.forward
-// (turbo.py:508-510, 531-538) and AceStepDiTModel.forward (turbo.py:1495-1500) do.
-template <int W, int NCH>
+// (turbo.py:508-510, 531-538) and AceStepDiTModel.forward (turbo.py:1495-1500) do, then
+// quantised per row.  Block-per-lane geometry of RowQ<D>: every load of the lane (x, norm
+// weight, modulation) is issued before the first reduction.
+template <int D, bool MUL, bool ADD>
 __global__ void __launch_bounds__(256) adanorm_quant_kernel(const NormArgs a) {
-  using G = RowGeo<W, NCH>;
-  constexpr int64_t D = G::kD;
+  using G = RowQ<D>;
   __shared__ float red[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wr = warp % W;
-  const int64_t m = (int64_t)blockIdx.x * G::kRowsPerCta + warp / W;
+  const int wr = warp % G::W;
+  const int64_t m = (int64_t)blockIdx.x * G::R + warp / G::W;
   const bool pad = m >= a.M;
-  const int64_t cbase = (int64_t)wr * 32 * NCH;
-  uint4 v[NCH];
-  float ss = 0.0f;
-  if (!pad) {
-    const uint4* row = reinterpret_cast<const uint4*>(a.x + m * a.ldx);
+  const bool lane_ok = G::kBPR >= 32 || lane < G::kBPR;
+  const bool live = !pad && lane_ok;
+  const uint4* row = reinterpret_cast<const uint4*>(a.x + (pad ? 0 : m) * a.ldx);
+  const int64_t mb = (pad ? 0 : m / a.rows_per_mod) * a.ld_mod;
+  const uint4* srow = reinterpret_cast<const uint4*>(a.scale1 + mb);
+  const uint4* hrow = reinterpret_cast<const uint4*>(a.shift + mb);
+  const uint4* wrow = reinterpret_cast<const uint4*>(a.norm_w);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  uint4 xv[2 * G::NB], wv[2 * G::NB], sv[2 * G::NB], hv[2 * G::NB];
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) v[j] = __ldg(row + cbase + 32 * j + lane);
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t c = 2 * ((int64_t)(wr * G::NB + j) * 32 + lane);
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ss = __fadd_rn(ss, __fmul_rn(bf16_lo(w4[i]), bf16_lo(w4[i])));
-        ss = __fadd_rn(ss, __fmul_rn(bf16_hi(w4[i]), bf16_hi(w4[i])));
-      }
+    for (int h = 0; h < 2; ++h) {
+      xv[2 * j + h] = live ? __ldg(row + c + h) : z;
+      wv[2 * j + h] = live ? __ldg(wrow + c + h) : z;
+      sv[2 * j + h] = (MUL && live) ? __ldg(srow + c + h) : z;
+      hv[2 * j + h] = (ADD && live) ? __ldg(hrow + c + h) : z;
     }
   }
-  ss = row_reduce<W, false>(ss, red, warp, lane);
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
+  ss = row_reduce<G::W, false>(ss, red, warp, lane);
   const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
   float am = 0.0f;
-  if (!pad) {
-    const uint4* wrow = reinterpret_cast<const uint4*>(a.norm_w);
-    const int64_t mb = a.scale1 ? (m / a.rows_per_mod) * a.ld_mod : 0;
-    const uint4* srow = a.scale1 ? reinterpret_cast<const uint4*>(a.scale1 + mb) : nullptr;
-    const uint4* hrow = a.shift ? reinterpret_cast<const uint4*>(a.shift + mb) : nullptr;
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      const int64_t c = cbase + 32 * j + lane;
-      const uint4 wv = __ldg(wrow + c);
-      const uint32_t xw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t sw[4] = {0u, 0u, 0u, 0u}, hw[4] = {0u, 0u, 0u, 0u};
-      if (srow) {
-        const uint4 sv = __ldg(srow + c);
-        sw[0] = sv.x, sw[1] = sv.y, sw[2] = sv.z, sw[3] = sv.w;
-      }
-      if (hrow) {
-        const uint4 hv = __ldg(hrow + c);
-        hw[0] = hv.x, hw[1] = hv.y, hw[2] = hv.z, hw[3] = hv.w;
-      }
-      uint32_t o[4];
+  for (int j = 0; j < 2 * G::NB; ++j) {
+    xv[j] = norm8<MUL, ADD>(xv[j], wv[j], sv[j], hv[j], rinv);
+    am = fmaxf(am, amax8(xv[j]));
+  }
+  if (a.y && live) {
+    uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float lo = bf16r(__fmul_rn(bf16_lo(xw[i]), rinv));
-        float hi = bf16r(__fmul_rn(bf16_hi(xw[i]), rinv));
-        lo = bf16r(__fmul_rn(bf16_lo(ww[i]), lo));
-        hi = bf16r(__fmul_rn(bf16_hi(ww[i]), hi));
-        if (srow) {
-          lo = bf16r(__fmul_rn(lo, bf16_lo(sw[i])));
-          hi = bf16r(__fmul_rn(hi, bf16_hi(sw[i])));
-        }
-        if (hrow) {
-          lo = bf16r(__fadd_rn(lo, bf16_lo(hw[i])));
-          hi = bf16r(__fadd_rn(hi, bf16_hi(hw[i])));
-        }
-        o[i] = pack_bf16(lo, hi);
-      }
-      v[j] = make_uint4(o[0], o[1], o[2], o[3]);
-      am = fmaxf(am, amax8(v[j]));
-      if (a.y) reinterpret_cast<uint4*>(a.y + m * a.ldy)[c] = v[j];
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t c = 2 * ((int64_t)(wr * G::NB + j) * 32 + lane);
+      yrow[c] = xv[2 * j];
+      yrow[c + 1] = xv[2 * j + 1];
     }
   }
   if (!a.codes) return;
-  am = row_reduce<W, true>(am, red, warp, lane);
+  am = row_reduce<G::W, true>(am, red, warp, lane);
   if (m >= a.Mpad) return;
   const int64_t r = m & 127;
   uint8_t* sf_rowbase = a.sf + (m >> 7) * (D / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
   if (pad) {  // padding rows of the scale layout: zero scales
-    for (int64_t c = wr * 32 + lane; c < D / 64; c += 32 * W) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+    for (int64_t c = wr * 32 + lane; c < D / 64; c += 32 * G::W) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
     return;
   }
   const float g = global_scale(am);
   if (wr == 0 && lane == 0) a.gs[m] = g;
   const float denom = __fmul_rn(6.0f, g);
-  uint32_t* code_row = reinterpret_cast<uint32_t*>(a.codes + m * (D / 2));
+  uint8_t* code_row = a.codes + m * (D / 2);
 #pragma unroll
-  for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, cbase + 32 * j + lane, lane, g, denom, code_row, sf_rowbase);
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+    store_block(quant_block(xv[2 * j], xv[2 * j + 1], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+  }
 }
 
 struct SiluArgs {
@@ -162,59 +154,69 @@ struct SiluArgs {
   uint8_t* sf;
 };
 
+__device__ __forceinline__ uint4 silu_mul8(uint4 g, uint4 u) {
+  const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float g0 = bf16_lo(gw[i]), g1 = bf16_hi(gw[i]);
+    // silu(g) = g / (1 + exp(-g)) with the hardware exp / divide approximations: the result is
+    // rounded to bf16 (8 mantissa bits), far coarser than their error
+    const float s0 = bf16r(__fdividef(g0, 1.0f + __expf(-g0)));
+    const float s1 = bf16r(__fdividef(g1, 1.0f + __expf(-g1)));
+    o[i] = pack_bf16(__fmul_rn(s0, bf16_lo(uw[i])), __fmul_rn(s1, bf16_hi(uw[i])));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // h = bf16(bf16(silu(gate)) * up) (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), turbo.py:34-35),
 // quantised per row for down_proj.
-template <int W, int NCH>
+template <int F>
 __global__ void __launch_bounds__(256) silu_mul_quant_kernel(const SiluArgs a) {
-  using G = RowGeo<W, NCH>;
-  constexpr int64_t F = G::kD;
+  using G = RowQ<F>;
   __shared__ float red[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wr = warp % W;
-  const int64_t m = (int64_t)blockIdx.x * G::kRowsPerCta + warp / W;
+  const int wr = warp % G::W;
+  const int64_t m = (int64_t)blockIdx.x * G::R + warp / G::W;
   const bool pad = m >= a.M;
-  const int64_t cbase = (int64_t)wr * 32 * NCH;
-  uint4 v[NCH];
-  float am = 0.0f;
-  if (!pad) {
-    const uint4* grow = reinterpret_cast<const uint4*>(a.gu + m * a.ld);
-    const uint4* urow = reinterpret_cast<const uint4*>(a.gu + m * a.ld + F);
-    uint4 gv[NCH], uv[NCH];
+  const bool lane_ok = G::kBPR >= 32 || lane < G::kBPR;
+  const bool live = !pad && lane_ok;
+  const uint4* grow = reinterpret_cast<const uint4*>(a.gu + (pad ? 0 : m) * a.ld);
+  const uint4* urow = reinterpret_cast<const uint4*>(a.gu + (pad ? 0 : m) * a.ld + F);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  uint4 gv[2 * G::NB], uv[2 * G::NB];
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      gv[j] = __ldg(grow + cbase + 32 * j + lane);
-      uv[j] = __ldg(urow + cbase + 32 * j + lane);
-    }
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t c = 2 * ((int64_t)(wr * G::NB + j) * 32 + lane);
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      const uint32_t gw[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
-      const uint32_t uw[4] = {uv[j].x, uv[j].y, uv[j].z, uv[j].w};
-      uint32_t o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float g0 = bf16_lo(gw[i]), g1 = bf16_hi(gw[i]);
-        const float s0 = bf16r(__fdiv_rn(g0, __fadd_rn(1.0f, expf(-g0))));
-        const float s1 = bf16r(__fdiv_rn(g1, __fadd_rn(1.0f, expf(-g1))));
-        o[i] = pack_bf16(__fmul_rn(s0, bf16_lo(uw[i])), __fmul_rn(s1, bf16_hi(uw[i])));
-      }
-      v[j] = make_uint4(o[0], o[1], o[2], o[3]);
-      am = fmaxf(am, amax8(v[j]));
+    for (int h = 0; h < 2; ++h) {
+      gv[2 * j + h] = live ? __ldg(grow + c + h) : z;
+      uv[2 * j + h] = live ? __ldg(urow + c + h) : z;
     }
   }
-  am = row_reduce<W, true>(am, red, warp, lane);
+  float am = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 2 * G::NB; ++j) {
+    gv[j] = silu_mul8(gv[j], uv[j]);
+    am = fmaxf(am, amax8(gv[j]));
+  }
+  am = row_reduce<G::W, true>(am, red, warp, lane);
   if (m >= a.Mpad) return;
   const int64_t r = m & 127;
   uint8_t* sf_rowbase = a.sf + (m >> 7) * (F / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
   if (pad) {
-    for (int64_t c = wr * 32 + lane; c < F / 64; c += 32 * W) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+    for (int64_t c = wr * 32 + lane; c < F / 64; c += 32 * G::W) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
     return;
   }
   const float g = global_scale(am);
   if (wr == 0 && lane == 0) a.gs[m] = g;
   const float denom = __fmul_rn(6.0f, g);
-  uint32_t* code_row = reinterpret_cast<uint32_t*>(a.codes + m * (F / 2));
+  uint8_t* code_row = a.codes + m * (F / 2);
 #pragma unroll
-  for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, cbase + 32 * j + lane, lane, g, denom, code_row, sf_rowbase);
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+    store_block(quant_block(gv[2 * j], gv[2 * j + 1], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+  }
 }
 
 struct HeadArgs {
@@ -269,37 +271,44 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const HeadArgs a) {
   *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]));
 }
 
-#define DEMON_ROW_CASE(KERN, W, NCH)                                                   \
-  case (W) * 256 * (NCH): {                                                            \
-    const dim3 grid((unsigned)((Mpad + RowGeo<W, NCH>::kRowsPerCta - 1) / RowGeo<W, NCH>::kRowsPerCta)); \
-    KERN<W, NCH><<<grid, 256, 0, st>>>(a);                                             \
-    return DEMON_OK;                                                                   \
-  }
+template <int D>
+void launch_adanorm_d(const NormArgs& a, cudaStream_t st) {
+  const dim3 grid((unsigned)((a.Mpad + RowQ<D>::R - 1) / RowQ<D>::R));
+  if (a.scale1 && a.shift) adanorm_quant_kernel<D, true, true><<<grid, 256, 0, st>>>(a);
+  else if (a.scale1) adanorm_quant_kernel<D, true, false><<<grid, 256, 0, st>>>(a);
+  else if (a.shift) adanorm_quant_kernel<D, false, true><<<grid, 256, 0, st>>>(a);
+  else adanorm_quant_kernel<D, false, false><<<grid, 256, 0, st>>>(a);
+}
 
-int launch_adanorm(int64_t D, int64_t Mpad, const NormArgs& a, cudaStream_t st) {
+int launch_adanorm(int64_t D, const NormArgs& a, cudaStream_t st) {
   switch (D) {
-    DEMON_ROW_CASE(adanorm_quant_kernel, 1, 1)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 2, 1)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 1)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 2)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 3)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 4)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 6)
-    DEMON_ROW_CASE(adanorm_quant_kernel, 4, 8)
+    case 256: launch_adanorm_d<256>(a, st); return DEMON_OK;
+    case 512: launch_adanorm_d<512>(a, st); return DEMON_OK;
+    case 1024: launch_adanorm_d<1024>(a, st); return DEMON_OK;
+    case 2048: launch_adanorm_d<2048>(a, st); return DEMON_OK;
+    case 3072: launch_adanorm_d<3072>(a, st); return DEMON_OK;
+    case 4096: launch_adanorm_d<4096>(a, st); return DEMON_OK;
+    case 6144: launch_adanorm_d<6144>(a, st); return DEMON_OK;
+    case 8192: launch_adanorm_d<8192>(a, st); return DEMON_OK;
     default: return DEMON_ERR_INVALID;
   }
 }
 
-int launch_silu(int64_t F, int64_t Mpad, const SiluArgs& a, cudaStream_t st) {
+template <int F>
+void launch_silu_f(const SiluArgs& a, cudaStream_t st) {
+  silu_mul_quant_kernel<F><<<(unsigned)((a.Mpad + RowQ<F>::R - 1) / RowQ<F>::R), 256, 0, st>>>(a);
+}
+
+int launch_silu(int64_t F, const SiluArgs& a, cudaStream_t st) {
   switch (F) {
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 1, 1)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 2, 1)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 1)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 2)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 3)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 4)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 6)
-    DEMON_ROW_CASE(silu_mul_quant_kernel, 4, 8)
+    case 256: launch_silu_f<256>(a, st); return DEMON_OK;
+    case 512: launch_silu_f<512>(a, st); return DEMON_OK;
+    case 1024: launch_silu_f<1024>(a, st); return DEMON_OK;
+    case 2048: launch_silu_f<2048>(a, st); return DEMON_OK;
+    case 3072: launch_silu_f<3072>(a, st); return DEMON_OK;
+    case 4096: launch_silu_f<4096>(a, st); return DEMON_OK;
+    case 6144: launch_silu_f<6144>(a, st); return DEMON_OK;
+    case 8192: launch_silu_f<8192>(a, st); return DEMON_OK;
     default: return DEMON_ERR_INVALID;
   }
 }
@@ -344,7 +353,7 @@ extern "C" int demon_adanorm_quantize(const void* x, int64_t M, int64_t D, int64
   a.y = reinterpret_cast<__nv_bfloat16*>(y);
   a.ldy = ldy;
   if (a.Mpad == 0) return DEMON_OK;
-  DEMON_CHECK_ARG(launch_adanorm(D, a.Mpad, a, reinterpret_cast<cudaStream_t>(stream)) == DEMON_OK,
+  DEMON_CHECK_ARG(launch_adanorm(D, a, reinterpret_cast<cudaStream_t>(stream)) == DEMON_OK,
                   "adanorm: unsupported width %lld", (long long)D);
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;
@@ -366,7 +375,7 @@ extern "C" int demon_silu_mul_quantize(const void* gu, int64_t M, int64_t F, int
   a.codes = codes;
   a.sf = sf;
   if (a.Mpad == 0) return DEMON_OK;
-  DEMON_CHECK_ARG(launch_silu(F, a.Mpad, a, reinterpret_cast<cudaStream_t>(stream)) == DEMON_OK,
+  DEMON_CHECK_ARG(launch_silu(F, a, reinterpret_cast<cudaStream_t>(stream)) == DEMON_OK,
                   "silu_mul: unsupported width %lld", (long long)F);
   DEMON_CUDA(cudaGetLastError());
   return DEMON_OK;

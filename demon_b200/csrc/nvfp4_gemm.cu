@@ -58,6 +58,14 @@ struct GemmParams {
   int a_gs_per_row;
   int w_gs_per_block;  // w_gs[n / 128] instead of w_gs[0]
   int lora_rank;
+  // per-head RMSNorm (+ RoPE) epilogue: heads of 128 in columns [0, hn_cols)
+  int hn_cols, hn_q_cols;
+  int64_t rope_S;
+  const __nv_bfloat16* hn_wq;
+  const __nv_bfloat16* hn_wk;
+  const __nv_bfloat16* rope_cos;
+  const __nv_bfloat16* rope_sin;
+  float hn_eps;
   int m_tiles, n_tiles;
 };
 
@@ -81,7 +89,8 @@ struct GemmCfg {
   static constexpr int kStgWarp = FP4 ? 4096 : 32 * kStgPitch;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
   static constexpr int offCol = offStg + kEpiWarps * kStgWarp;  // fp32 per-column vector per warp
-  static constexpr int offBar = offCol + kEpiWarps * (BN / 2) * 4;
+  static constexpr int offHn = offCol + kEpiWarps * (BN / 2) * 4;  // fp32 head-norm weight per warp
+  static constexpr int offBar = offHn + (FP4 ? kEpiWarps * (BN / 2) * 4 : 0);
   static constexpr int kBars = 2 * STAGES + 3;
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
@@ -276,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // which half of the tile's columns
     const uint32_t stg = smem_u32(smem + C::offStg + ew * C::kStgWarp);
     const uint32_t colv = smem_u32(smem + C::offCol) + ew * (C::kColsPerWarp * 4);
+    const uint32_t hnv = smem_u32(smem + C::offHn) + ew * (C::kColsPerWarp * 4);
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     uint32_t it = 0, nstore = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
@@ -291,6 +301,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n < p.N)
           cv = (FP4 || !p.col_scale) ? (p.bias ? __bfloat162float(p.bias[n]) : 0.0f) : p.col_scale[n];
         st_shared_f32(colv + 4 * i, cv);
+      }
+      // a BN = 256 warp owns one 128-column head: stage its norm weight
+      const bool hn = FP4 && BN == 256 && ncol0 < p.hn_cols;
+      if (hn) {  // as bf16 pairs: word i holds columns 2i, 2i + 1
+        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(ncol0 < p.hn_q_cols ? p.hn_wq : p.hn_wk);
+        for (int i = lane; i < C::kColsPerWarp / 2; i += 32)
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(hnv + 4 * i), "r"(__ldg(wsrc + i)) : "memory");
       }
       const int64_t row = (int64_t)m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
@@ -329,10 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 8; ++j) {
           const float4 cv = ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j));
           if (FP4) {
-            y[c][2 * j] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][4 * j]), cv.x),
-                                      fmaf(alpha, __uint_as_float(v[c][4 * j + 1]), cv.y));
-            y[c][2 * j + 1] = pack_bf16x2(fmaf(alpha, __uint_as_float(v[c][4 * j + 2]), cv.z),
-                                          fmaf(alpha, __uint_as_float(v[c][4 * j + 3]), cv.w));
+            const float2 al = make_float2(alpha, alpha);
+            y[c][2 * j] = f2_bf2(fma_f2(al, make_float2(__uint_as_float(v[c][4 * j]), __uint_as_float(v[c][4 * j + 1])),
+                                        make_float2(cv.x, cv.y)));
+            y[c][2 * j + 1] = f2_bf2(fma_f2(
+                al, make_float2(__uint_as_float(v[c][4 * j + 2]), __uint_as_float(v[c][4 * j + 3])),
+                make_float2(cv.z, cv.w)));
           } else if (plain) {
             y[c][2 * j] = pack_bf16x2(__uint_as_float(v[c][4 * j]) + cv.x, __uint_as_float(v[c][4 * j + 1]) + cv.y);
             y[c][2 * j + 1] =
@@ -346,6 +365,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
+      if (hn) {
+        // q_norm / k_norm: Qwen3RMSNorm over the row's 128 values of this head
+        float2 s2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float2 f = bf2_f2(y[c][k]);
+            s2 = fma_f2(f, f, s2);
+          }
+        const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(__fadd_rn(s2.x, s2.y), 128.0f), p.hn_eps));
+        const float2 r2 = make_float2(rinv, rinv);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w4 = ld_shared_v4(hnv + 4 * (c * 16 + 4 * j));
+            const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)  // bf16(w * bf16(y * rinv))
+              y[c][4 * j + i] = mul_bf2(f2_bf2(mul_f2(bf2_f2(y[c][4 * j + i]), r2)), ww[i]);
+          }
+        if (p.rope_cos) {
+          // bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)): column i < 64 pairs with i + 64
+          const int64_t pos = row % p.rope_S;
+          const uint4* cr = reinterpret_cast<const uint4*>(p.rope_cos + pos * 128);
+          const uint4* sr = reinterpret_cast<const uint4*>(p.rope_sin + pos * 128);
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 c1 = __ldg(cr + c * 4 + j), c2 = __ldg(cr + 8 + c * 4 + j);
+              const uint4 s1 = __ldg(sr + c * 4 + j), s2v = __ldg(sr + 8 + c * 4 + j);
+              const uint32_t cw1[4] = {c1.x, c1.y, c1.z, c1.w}, cw2[4] = {c2.x, c2.y, c2.z, c2.w};
+              const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w}, sw2[4] = {s2v.x, s2v.y, s2v.z, s2v.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t a = y[c][4 * j + i], b = y[c + 2][4 * j + i];
+                y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(mul_bf2(a, cw1[i])), bf2_f2(mul_bf2(b ^ 0x80008000u, sw1[i]))));
+                y[c + 2][4 * j + i] = f2_bf2(add_f2(bf2_f2(mul_bf2(b, cw2[i])), bf2_f2(mul_bf2(a, sw2[i]))));
+              }
+            }
+        }
+      }
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
         const int ncol = ncol0 + c * 32;
@@ -359,9 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 4; ++j) {
               const uint32_t gw[4] = {gx[j].x, gx[j].y, gx[j].z, gx[j].w};
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                y[c][4 * j + i] = pack_bf16x2(bf16_lo(y[c][4 * j + i]) * bf16_lo(gw[i]),
-                                              bf16_hi(y[c][4 * j + i]) * bf16_hi(gw[i]));
+              for (int i = 0; i < 4; ++i) y[c][4 * j + i] = mul_bf2(y[c][4 * j + i], gw[i]);
             }
           }
           if (res_row) {  // out = bf16(residual + y)
@@ -371,9 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 4; ++j) {
               const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                y[c][4 * j + i] = pack_bf16x2(bf16_lo(rw[i]) + bf16_lo(y[c][4 * j + i]),
-                                              bf16_hi(rw[i]) + bf16_hi(y[c][4 * j + i]));
+              for (int i = 0; i < 4; ++i) y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(y[c][4 * j + i])));
             }
           }
           // 32 rows x 32 columns, 64-byte swizzle (conflict-free), written by one TMA store;
@@ -484,6 +543,17 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                   "gemm: LoRA needs lora_b and rank %% 16 == 0, 0 < rank <= 128 (rank=%lld)",
                   (long long)a->lora_rank);
   DEMON_CHECK_ARG(!(lora && a->w_gs_per_block), "gemm: hot LoRA needs a single weight scale (w_gs_per_block = 0)");
+  if (a->hn_cols > 0) {
+    DEMON_CHECK_ARG(N % 256 == 0 && a->hn_cols % 128 == 0 && a->hn_cols <= N && a->hn_q_cols >= 0 &&
+                        a->hn_q_cols % 128 == 0 && a->hn_q_cols <= a->hn_cols,
+                    "gemm: head norm needs N %% 256 == 0 and hn_q_cols <= hn_cols <= N, both multiples of 128");
+    DEMON_CHECK_ARG(!a->gate && !a->residual, "gemm: head norm excludes gate / residual");
+    DEMON_CHECK_ARG((a->hn_q_cols == 0 || a->hn_wq) && (a->hn_q_cols == a->hn_cols || a->hn_wk),
+                    "gemm: head norm weight missing");
+    DEMON_CHECK_ARG(!a->rope_cos || (a->rope_sin && a->rope_S > 0 && ((uintptr_t)a->rope_cos & 15) == 0 &&
+                                     ((uintptr_t)a->rope_sin & 15) == 0),
+                    "gemm: rotary tables need rope_sin, rope_S > 0 and 16-byte alignment");
+  }
   if (M == 0) return DEMON_OK;
 
   const bool bn256 = (N % 256 == 0);
@@ -523,6 +593,14 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.K = (int)K;
   p.a_gs_per_row = a->a_gs_per_row;
   p.w_gs_per_block = a->w_gs_per_block;
+  p.hn_cols = (int)a->hn_cols;
+  p.hn_q_cols = (int)a->hn_q_cols;
+  p.rope_S = a->rope_S > 0 ? a->rope_S : 1;
+  p.hn_wq = reinterpret_cast<const __nv_bfloat16*>(a->hn_wq);
+  p.hn_wk = reinterpret_cast<const __nv_bfloat16*>(a->hn_wk);
+  p.rope_cos = reinterpret_cast<const __nv_bfloat16*>(a->rope_cos);
+  p.rope_sin = reinterpret_cast<const __nv_bfloat16*>(a->rope_sin);
+  p.hn_eps = a->hn_eps;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);

@@ -12,11 +12,11 @@
 //   code  = e2m1_rne(x * (1 / (f32(s_b) * g)))      saturating at 6, zero -> code 0
 // The absmax floor 1e-12 is the reference's FP8 floor (acestep/engine/trt/fp8_onnx.py:67).
 //
-// Layout of the work: one warp per row.  Lane l owns the 8-element chunks
-// l + 32 j (one 128-bit load each), so lanes (2i, 2i+1) hold one 16-element
-// block; the block absmax is one shuffle.  Codes of a chunk are one 32-bit
-// store (a warp writes 128 contiguous bytes); four block scales that are
-// contiguous in the scale layout are gathered by shuffles into one 32-bit store.
+// Layout of the work (fast path): each lane owns whole 16-element blocks (two 128-bit
+// loads); a block's codes are one 64-bit store (a warp writes 256 contiguous bytes) and
+// the four block scales that are contiguous in the scale layout are gathered by
+// shuffles into one 32-bit store.  Other widths: one warp per row, lanes (2i, 2i+1)
+// share a block.
 #include <algorithm>
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
@@ -95,30 +95,34 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16* __re
   }
 }
 
-// Fast path for K = NCH * 1024: a row is split over kRowWarps warps (each lane
-// holds NCH 128-bit chunks in registers, all loads in flight at once); the
-// per-row absmax is combined through shared memory.  Two rows per 256-thread CTA.
-constexpr int kRowWarps = 4;
-template <int GS_MODE, int NCH>
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t M,
-                                                            int64_t ldx, int64_t Mpad, float* __restrict__ gs,
-                                                            uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
-  constexpr int64_t K = (int64_t)NCH * 1024;
-  constexpr int kRowsPerCta = 8 / kRowWarps;
+// Fast path for the row widths of the DiT (K in {512, 1024, 2048, 3072, 4096, 6144, 8192}):
+// each lane owns whole 16-element scale blocks (two 128-bit loads per block, all loads of
+// the lane in flight at once), so a block's scale is computed once; a row is held by W
+// warps whose per-row absmax meets in shared memory; 8 / W rows per 256-thread CTA.
+template <int GS_MODE, int K>
+__global__ void __launch_bounds__(256) quantize_blocks_kernel(const __nv_bfloat16* __restrict__ x, int64_t M,
+                                                              int64_t ldx, int64_t Mpad, float* __restrict__ gs,
+                                                              uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  using G = RowQ<K>;
   __shared__ float red[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wr = warp % kRowWarps;
-  const int64_t m = (int64_t)blockIdx.x * kRowsPerCta + warp / kRowWarps;
+  const int wr = warp % G::W;
+  const int64_t m = (int64_t)blockIdx.x * G::R + warp / G::W;
   const int64_t r = m & 127;
   uint8_t* sf_rowbase = sf + (m >> 7) * (K / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
   const bool pad = m >= M;
   const uint4* row = reinterpret_cast<const uint4*>(x + (pad ? 0 : m) * ldx);
-  uint32_t* code_row = reinterpret_cast<uint32_t*>(codes + (pad ? 0 : m) * (K / 2));
-  const int64_t cbase = (int64_t)wr * 32 * NCH;  // this warp's first 8-element chunk
-  uint4 v[NCH];
-  if (!pad) {
+  const bool lane_ok = G::kBPR >= 32 || lane < G::kBPR;
+  uint4 a[G::NB], b[G::NB];
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) v[j] = __ldg(row + cbase + 32 * j + lane);
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+    if (!pad && lane_ok) {
+      a[j] = __ldg(row + 2 * kb);
+      b[j] = __ldg(row + 2 * kb + 1);
+    } else {
+      a[j] = b[j] = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   float g = 0.0f;
   if (GS_MODE == 0) {
@@ -126,43 +130,44 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
   } else if (GS_MODE == 1) {
     g = global_scale(gs[0]);
   } else {
-    float a = 0.0f;
-    if (!pad) {
+    float am = 0.0f;
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) a = fmaxf(a, amax8(v[j]));
-    }
-    a = warp_max(a);
-    if (lane == 0) red[warp] = a;
-    __syncthreads();
-    const int w0 = warp - wr;
-    float am = red[w0];
-#pragma unroll
-    for (int i = 1; i < kRowWarps; ++i) am = fmaxf(am, red[w0 + i]);
-    g = global_scale(am);
+    for (int j = 0; j < G::NB; ++j) am = fmaxf(am, fmaxf(amax8(a[j]), amax8(b[j])));
+    g = global_scale(row_reduce<G::W, true>(am, red, warp, lane));
     if (wr == 0 && lane == 0 && !pad) gs[m] = g;
   }
   if (m >= Mpad) return;
   if (pad) {  // padding rows of the scale layout: zero scales
-    for (int64_t c = wr * 32 + lane; c < K / 64; c += 32 * kRowWarps)
-      *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+    for (int64_t c = wr * 32 + lane; c < K / 64; c += 32 * G::W) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
     return;
   }
   const float denom = __fmul_rn(6.0f, g);
+  uint8_t* code_row = codes + m * (K / 2);
 #pragma unroll
-  for (int j = 0; j < NCH; ++j) quant_chunk(v[j], true, cbase + 32 * j + lane, lane, g, denom, code_row, sf_rowbase);
+  for (int j = 0; j < G::NB; ++j) {
+    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+    store_block(quant_block(a[j], b[j], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+  }
+}
+
+template <int GS_MODE, int K>
+void launch_blocks(cudaStream_t st, const __nv_bfloat16* x, int64_t M, int64_t ldx, int64_t Mpad, float* gs,
+                   uint8_t* codes, uint8_t* sf) {
+  constexpr int R = RowQ<K>::R;
+  quantize_blocks_kernel<GS_MODE, K><<<(unsigned)((Mpad + R - 1) / R), 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf);
 }
 
 template <int GS_MODE>
 void launch_quantize(cudaStream_t st, const __nv_bfloat16* x, int64_t M, int64_t K, int64_t ldx, int64_t Mpad,
                      float* gs, uint8_t* codes, uint8_t* sf) {
-  const dim3 grid_rows((unsigned)((Mpad + 1) / 2));  // two rows per CTA
   switch (K) {
-    case 1024: quantize_rows_kernel<GS_MODE, 1><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
-    case 2048: quantize_rows_kernel<GS_MODE, 2><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
-    case 3072: quantize_rows_kernel<GS_MODE, 3><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
-    case 4096: quantize_rows_kernel<GS_MODE, 4><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
-    case 6144: quantize_rows_kernel<GS_MODE, 6><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
-    case 8192: quantize_rows_kernel<GS_MODE, 8><<<grid_rows, 256, 0, st>>>(x, M, ldx, Mpad, gs, codes, sf); return;
+    case 512: launch_blocks<GS_MODE, 512>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 1024: launch_blocks<GS_MODE, 1024>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 2048: launch_blocks<GS_MODE, 2048>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 3072: launch_blocks<GS_MODE, 3072>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 4096: launch_blocks<GS_MODE, 4096>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 6144: launch_blocks<GS_MODE, 6144>(st, x, M, ldx, Mpad, gs, codes, sf); return;
+    case 8192: launch_blocks<GS_MODE, 8192>(st, x, M, ldx, Mpad, gs, codes, sf); return;
     default: {
       const dim3 grid((unsigned)((Mpad + kQuantWarps - 1) / kQuantWarps));
       quantize_kernel<GS_MODE><<<grid, 256, 0, st>>>(x, M, K, ldx, Mpad, gs, codes, sf);

@@ -69,6 +69,12 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // One 8-element chunk of a row: block absmax (lanes 2i, 2i+1), scale, codes,
 // and the 32-bit scale-group store (lanes with lane % 8 == 0).  Every lane of
 // the warp calls this (the shuffles need the full warp); `valid` masks stores.
@@ -91,10 +97,76 @@ __device__ __forceinline__ void quant_chunk(uint4 v, bool valid, int64_t c, int 
   }
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+// E4M3 byte -> float through the hardware conversion (exact: every E4M3 value, subnormals
+// included, is an FP16 value).
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  uint32_t h2;
+  asm("{\n\t.reg .b16 s;\n\tcvt.u16.u32 s, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, s;\n\t}" : "=r"(h2) : "r"(b & 0xFFu));
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
 }
+
+// One 16-element scale block held by one lane (two 8-element chunks): block scale byte
+// and 64 bits of codes (same arithmetic as quant_chunk, without the pair exchange).
+struct QBlock {
+  uint2 codes;
+  uint32_t sb;
+};
+__device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float denom) {
+  const float am = fmaxf(amax8(a), amax8(b));
+  const float s = fminf(__fdiv_rn(am, denom), 448.0f);
+  QBlock q;
+  q.sb = e4m3_rne_sat(s);
+  q.codes = make_uint2(0u, 0u);
+  const float sbf = e4m3_to_f32(q.sb);
+  if (sbf != 0.0f) {
+    const float rs = __frcp_rn(__fmul_rn(sbf, g));
+    q.codes = make_uint2(pack8(a, rs), pack8(b, rs));
+  }
+  return q;
+}
+
+// Lane owns scale block kb of row m (K/16 blocks per row): store its 8 code bytes and, from
+// lanes with kb % 4 == 0, the four consecutive scale bytes of the tcgen05 layout as one word.
+// All 32 lanes must call it (shuffles); `valid` masks the stores.
+__device__ __forceinline__ void store_block(const QBlock& q, bool valid, int64_t kb, int lane, uint8_t* code_row,
+                                            uint8_t* sf_rowbase) {
+  const uint32_t s1 = __shfl_down_sync(0xffffffffu, q.sb, 1);
+  const uint32_t s2 = __shfl_down_sync(0xffffffffu, q.sb, 2);
+  const uint32_t s3 = __shfl_down_sync(0xffffffffu, q.sb, 3);
+  if (valid) {
+    reinterpret_cast<uint2*>(code_row)[kb] = q.codes;
+    if ((lane & 3) == 0)
+      *reinterpret_cast<uint32_t*>(sf_rowbase + (kb >> 2) * 512) = q.sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
+// Geometry of the block-per-lane row kernels for a row of K elements: W warps per row, NB
+// blocks per lane; lane l of row-warp w owns blocks kb = (w * NB + j) * 32 + l (j < NB).
+// Rows shorter than 512 use the first K/16 lanes of one warp.
+template <int K>
+struct RowQ {
+  static constexpr int kBPR = K / 16;
+  static constexpr int W = (kBPR % 128 == 0) ? 4 : (kBPR % 64 == 0) ? 2 : 1;
+  static constexpr int NB = kBPR >= 32 * W ? kBPR / (32 * W) : 1;
+  static constexpr int R = 8 / W;  // rows per 256-thread CTA
+  static_assert(kBPR % 4 == 0 && (kBPR < 32 || kBPR % (32 * W) == 0), "row width");
+};
+
+// Cross-warp reduction of one value per row (sum or max): full-warp shuffle, then the W
+// warps of a row combine through shared memory (all threads of the CTA must call it).
+template <int W, bool MAX>
+__device__ __forceinline__ float row_reduce(float v, float* red, int warp, int lane) {
+  v = MAX ? warp_max(v) : warp_sum(v);
+  if (W == 1) return v;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int w0 = warp - warp % W;
+  float r = red[w0];
+#pragma unroll
+  for (int i = 1; i < W; ++i) r = MAX ? fmaxf(r, red[w0 + i]) : r + red[w0 + i];
+  return r;
+}
+
 
 }  // namespace demon

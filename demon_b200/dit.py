@@ -11,11 +11,13 @@ Data path of one layer (M = B * S rows of the residual stream ``h``):
 
 * ``demon_adanorm_quantize``: RMSNorm + AdaLN modulation written straight into the
   NVFP4 operand (the normalised bf16 activation is never stored);
-* one NVFP4 GEMM for q/k/v (packed weights concatenated, each with its own scale),
-  ``demon_head_norm_rope`` in place on q and k, attention, then the activation
-  quantiser and the o_proj GEMM whose epilogue applies the AdaLN gate and residual;
-* cross-attention: RMSNorm -> NVFP4 -> q GEMM, q_norm; the encoder K/V of all layers
-  come from one quantised copy of the embedded encoder states;
+* one NVFP4 GEMM for q/k/v (packed weights concatenated, each with its own scale) whose
+  epilogue applies q_norm / k_norm and the rotary embedding per 128-column head, attention,
+  then the activation quantiser and the o_proj GEMM whose epilogue applies the AdaLN gate
+  and residual;
+* cross-attention: RMSNorm -> NVFP4 -> q GEMM (q_norm in its epilogue); the encoder K/V
+  (k_norm in the epilogue) of all layers come from one quantised copy of the embedded
+  encoder states;
 * MLP: one GEMM for gate/up, ``demon_silu_mul_quantize``, down GEMM with gate + residual.
 
 Every DiT linear that the reference's low-precision export quantises (all but
@@ -37,7 +39,7 @@ from torch import nn
 
 from . import nvfp4 as Q
 from .nvfp4 import NVFP4Linear
-from .rowops import adanorm_quantize, head_norm_rope, silu_mul_quantize
+from .rowops import adanorm_quantize, silu_mul_quantize
 
 try:  # FlashAttention 2 (library): unsplit KV loop via flash_attn_with_kvcache(num_splits=1)
     from flash_attn import flash_attn_with_kvcache as _fa_kvcache
@@ -170,23 +172,36 @@ class Attention(nn.Module):
             self._fused = Q.fuse_weights([_packed(l) for l in parts])
         return self._fused
 
-    def _proj(self, lins, a, xb):
-        """Columns of the listed projections side by side: one fused GEMM, or one per linear
-        when any has a hot LoRA."""
+    def _norm_spec(self, lin):
+        """The head-norm epilogue of one projection: q_norm on q_proj, k_norm on k_proj."""
+        eps = self.q_norm.variance_epsilon
+        if lin is self.q_proj:
+            return (lin.out_features, lin.out_features, self.q_norm.weight, None, eps)
+        if lin is self.k_proj:
+            return (lin.out_features, 0, None, self.k_norm.weight, eps)
+        return None
+
+    def _proj(self, lins, a, xb, rope=None):
+        """Columns of the listed projections side by side, q/k heads normalised (and rotated
+        with ``rope``) in the GEMM epilogue: one fused GEMM, or one per linear when any has a
+        hot LoRA."""
         if not _has_lora(*lins):
-            return Q.gemm(a, self.fused() if len(lins) > 1 else _packed(lins[0]))
+            specs = [self._norm_spec(l) for l in lins]
+            hn_cols = sum(l.out_features for l, sp in zip(lins, specs) if sp is not None)
+            hn_q = sum(l.out_features for l in lins if l is self.q_proj)
+            hn = (hn_cols, hn_q, self.q_norm.weight, self.k_norm.weight, self.q_norm.variance_epsilon)
+            return Q.gemm(a, self.fused() if len(lins) > 1 else _packed(lins[0]), head_norm=hn, rope=rope)
         outs = []
         for l in lins:
             xa, lb = _lora(l, xb, a)
-            outs.append(Q.gemm(a, _packed(l), lora_xa=xa, lora_b=lb))
+            sp = self._norm_spec(l)
+            outs.append(Q.gemm(a, _packed(l), lora_xa=xa, lora_b=lb, head_norm=sp, rope=rope if sp else None))
         return torch.cat(outs, 1)
 
     def self_attn(self, a, xb, h, gate, B, S, rope):
         hd, hq, hk = self.head_dim, self.hq, self.hk
-        qkv = self._proj([self.q_proj, self.k_proj, self.v_proj], a, xb)       # [M, (hq + 2 hk) * hd]
         cos, sin = rope
-        head_norm_rope(qkv, 0, hq, self.q_norm.weight, self.q_norm.variance_epsilon, cos, sin, S)
-        head_norm_rope(qkv, hq * hd, hk, self.k_norm.weight, self.k_norm.variance_epsilon, cos, sin, S)
+        qkv = self._proj([self.q_proj, self.k_proj, self.v_proj], a, xb, rope=(cos, sin, S))  # [M, (hq+2hk)*hd]
         ld = qkv.stride(0)
         q = qkv.as_strided((B, S, hq, hd), (S * ld, ld, hd, 1))
         k = qkv.as_strided((B, S, hk, hd), (S * ld, ld, hd, 1), hq * hd)
@@ -196,15 +211,12 @@ class Attention(nn.Module):
 
     def cross_kv(self, enc_a, enc_b, B, L):
         """Encoder K (k_norm applied) and V of this layer: [B*L, 2 * hk * hd]."""
-        kv = self._proj([self.k_proj, self.v_proj], enc_a, enc_b)
-        head_norm_rope(kv, 0, self.hk, self.k_norm.weight, self.k_norm.variance_epsilon)
-        return kv
+        return self._proj([self.k_proj, self.v_proj], enc_a, enc_b)
 
     def cross_attn(self, a, xb, h, kv, B, S, L):
         hd, hq, hk = self.head_dim, self.hq, self.hk
         xa, lb = _lora(self.q_proj, xb, a)
-        q = Q.gemm(a, _packed(self.q_proj), lora_xa=xa, lora_b=lb)
-        head_norm_rope(q, 0, hq, self.q_norm.weight, self.q_norm.variance_epsilon)
+        q = Q.gemm(a, _packed(self.q_proj), lora_xa=xa, lora_b=lb, head_norm=self._norm_spec(self.q_proj))
         ld = kv.stride(0)
         k = kv.as_strided((B, L, hk, hd), (L * ld, ld, hd, 1))
         v = kv.as_strided((B, L, hk, hd), (L * ld, ld, hd, 1), hk * hd)

@@ -142,8 +142,14 @@ def lora_down(x: torch.Tensor, lora_a: torch.Tensor, col_scale: torch.Tensor, a:
 def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, gate_rows: int = 1,
          lora_xa: torch.Tensor | None = None, lora_b: torch.Tensor | None = None,
-         out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """out = residual + gate * (alpha * (A W^T + lora) + bias), bf16 [M, N]."""
+         out: torch.Tensor | None = None, head_norm: tuple | None = None, rope: tuple | None = None,
+         stream=None) -> torch.Tensor:
+    """out = residual + gate * (alpha * (A W^T + lora) + bias), bf16 [M, N].
+
+    ``head_norm = (hn_cols, hn_q_cols, w_q, w_k, eps)``: per-head RMSNorm of the output's
+    first hn_cols columns (heads of 128; w_q for the first hn_q_cols, w_k after), and with
+    ``rope = (cos, sin, S)`` the rotary embedding after it (q/k projections of the DiT).
+    """
     if a.K != w.K:
         raise ValueError(f"K mismatch: activations {a.K} vs weight {w.K}")
     M, N, K = a.rows, w.rows, a.K
@@ -164,6 +170,16 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
         args.gate, args.gate_rows, args.ld_gate = nat.ptr(gate), gate_rows, gate.stride(0)
     if lora_xa is not None:
         args.lora_xa, args.lora_b, args.lora_rank = nat.ptr(lora_xa), nat.ptr(lora_b), lora_xa.shape[1]
+    if head_norm is not None:
+        hn_cols, hn_q, wq, wk, eps = head_norm
+        for wt in (wq, wk):
+            if wt is not None and (wt.dtype != torch.bfloat16 or not wt.is_contiguous()):
+                raise ValueError("head-norm weights must be contiguous bf16 [128]")
+        args.hn_cols, args.hn_q_cols, args.hn_wq, args.hn_wk = hn_cols, hn_q, nat.ptr(wq), nat.ptr(wk)
+        args.hn_eps = float(eps)
+        if rope is not None:
+            cos, sin, S = rope
+            args.rope_cos, args.rope_sin, args.rope_S = nat.ptr(cos), nat.ptr(sin), int(S)
     nat.check(nat.load().demon_nvfp4_gemm(ctypes.byref(args), nat.stream_ptr(stream)))
     return out
 

@@ -119,6 +119,20 @@ typedef struct DemonGemmArgs {
   const void* lora_xa;    /* bf16 [M, lora_rank] or NULL */
   const void* lora_b;     /* bf16 [N, lora_rank] */
   int64_t lora_rank;
+  /* Per-head RMSNorm (+ rotary embedding) of the output, for q/k projections: output columns
+   * [0, hn_cols) form heads of 128; a head in [0, hn_q_cols) is normalised with weight hn_wq,
+   * the others with hn_wk (bf16 [128] each): y = bf16(w * bf16(y * rsqrt(mean(y^2) + hn_eps))),
+   * then, with rope_cos / rope_sin (bf16 [rope_S, 128], position = row % rope_S),
+   * y = bf16(bf16(y * cos) + bf16(rotate_half(y) * sin)) -- the q_norm / k_norm and
+   * apply_rotary_pos_emb of AceStepAttention.forward (turbo.py:311-345).  hn_cols = 0: off.
+   * Needs N % 256 == 0, no gate / residual. */
+  int64_t hn_cols, hn_q_cols, rope_S;
+  const void* hn_wq;
+  const void* hn_wk;
+  const void* rope_cos;
+  const void* rope_sin;
+  float hn_eps;
+  int32_t _pad1;
 } DemonGemmArgs;
 
 DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);

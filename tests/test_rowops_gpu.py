@@ -165,3 +165,31 @@ def test_bf16_linear(cuda, M, K, N):
     assert rel < 4e-3, rel  # bf16 output rounding: 2^-9 relative at most, ~1e-3 rms
     y1 = Q.bf16_linear(x[M - 1:].to(cuda), w.to(cuda), b.to(cuda))
     assert torch.equal(y1[0], y[M - 1])          # a row does not depend on the batch
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_gemm_head_norm_epilogue(cuda, rope):
+    """q/k head RMSNorm (+ RoPE) in the GEMM epilogue equals the GEMM followed by the
+    standalone head-norm kernel (same arithmetic; the sum of squares runs in another order)."""
+    from demon_b200 import nvfp4 as Q
+    from demon_b200.rowops import head_norm_rope
+    M, K, S, hq, hk = 300, 2048, 150, 4, 2
+    N = (hq + 2 * hk) * 128
+    g = torch.Generator().manual_seed(21)
+    x = make_x(M, K, 5).to(cuda)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    wq = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda)
+    wk = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda)
+    pos = torch.arange(S, dtype=torch.float32)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2).float() / 128))
+    emb = torch.cat([pos[:, None] * inv[None]] * 2, -1)
+    cos, sin = emb.cos().to(torch.bfloat16).to(cuda), emb.sin().to(torch.bfloat16).to(cuda)
+    a, pw = Q.quantize(x), Q.pack_weight(w)
+    rp = (cos, sin, S) if rope else None
+    fused = Q.gemm(a, pw, head_norm=((hq + hk) * 128, hq * 128, wq, wk, 1e-6), rope=rp)
+    ref = Q.gemm(a, pw)
+    kw = dict(cos=cos, sin=sin, S=S) if rope else {}
+    head_norm_rope(ref, 0, hq, wq, 1e-6, **kw)
+    head_norm_rope(ref, hq * 128, hk, wk, 1e-6, **kw)
+    ulp_check(fused[:, :(hq + hk) * 128], ref[:, :(hq + hk) * 128])
+    assert torch.equal(fused[:, (hq + hk) * 128:], ref[:, (hq + hk) * 128:])
