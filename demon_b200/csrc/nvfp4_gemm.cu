@@ -75,10 +75,10 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
-template <int BN, int STAGES, bool FP4>
+template <int BN, int STAGES, bool FP4, bool PAIR = false>
 struct GemmCfg {
   static constexpr int kA = kBM * kRowBytes;
-  static constexpr int kB = BN * kRowBytes;
+  static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
   static constexpr int kSFA = FP4 ? 2048 : 0;
   static constexpr int kSFB = FP4 ? ((BN + 127) / 128) * 2048 : 0;
   static constexpr int offA = 0;
@@ -118,12 +118,13 @@ __device__ __forceinline__ uint64_t sf_desc(const void* p) {
 // the TMA 64-byte swizzle (address bits [4,5] ^= bits [7,8]).
 __device__ __forceinline__ int stg_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
-template <int BN, int STAGES, bool FP4>
+template <int BN, int STAGES, bool FP4, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
-  using C = GemmCfg<BN, STAGES, FP4>;
+                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmSFA,
+                const __grid_constant__ CUtensorMap tmSFB, const GemmParams p) {
+  using C = GemmCfg<BN, STAGES, FP4, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::offBar);
@@ -139,6 +140,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lboxes = p.lora_rank > 0 ? (p.lora_rank + 63) / 64 : 0;
   const int num_tiles = p.m_tiles * p.n_tiles;
   const uint64_t t0 = globaltimer();
+  // CTA pair (cta_group::2): the pair computes a 256 x BN tile, CTA `rank` owns rows
+  // 128 * rank .. +128 of it and half of the B tile; the leader (rank 0) issues the MMAs.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int cid = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ncl = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int kTileM = PAIR ? 2 * kBM : kBM;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -146,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kEpiWarps);
+    mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);  // the pair's epilogue warps
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -158,13 +166,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmLA);
       prefetch_tmap(&tmLB);
     }
+    if (PAIR) {
+      prefetch_tmap(&tmSFA);
+      prefetch_tmap(&tmSFB);
+    }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::kTmemCols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_holder, C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrive / complete_tx
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
@@ -174,15 +194,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;  // stages issued so far (all tiles)
       const int64_t kchunks = p.K / 64;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = cid; ok && tile < num_tiles; tile += ncl) {
         const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
-        const int m0 = m_blk * kBM, n0 = n_blk * BN;
+        const int m0 = m_blk * kTileM, n0 = n_blk * BN;
+        const int am0 = m0 + (int)rank * kBM;                  // this CTA's A rows
+        const int bn0 = n0 + (int)rank * (BN / 2) * (PAIR ? 1 : 0);  // this CTA's B rows
+        // a pair's stage completes on the leader's barrier with both CTAs' bytes
+        const uint32_t mult = PAIR ? 2u : 1u;
         for (int b = 0; b < lboxes; ++b, ++g) {
           const int s = g % STAGES;
           if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 1))) break;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::kA + C::kB));
-          tma_load_2d(smem + C::offA + s * C::kA, &tmLA, &full[s], b * 64, m0);
-          tma_load_2d(smem + C::offB + s * C::kB, &tmLB, &full[s], b * 64, n0);
+          if (leader) mbar_arrive_expect_tx(&full[s], mult * (uint32_t)(C::kA + C::kB));
+          if (PAIR) {
+            tma_load_2d_pair(smem + C::offA + s * C::kA, &tmLA, &full[s], b * 64, am0);
+            tma_load_2d_pair(smem + C::offB + s * C::kB, &tmLB, &full[s], b * 64, bn0);
+          } else {
+            tma_load_2d(smem + C::offA + s * C::kA, &tmLA, &full[s], b * 64, am0);
+            tma_load_2d(smem + C::offB + s * C::kB, &tmLB, &full[s], b * 64, bn0);
+          }
         }
         // scale halves of the B tile that exist in the (128-row padded) scale buffer
         const int sfb_halves = FP4 ? std::min((BN + 127) / 128, (p.N - n0 + 127) / 128) : 0;
@@ -190,21 +219,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kt = 0; ok && kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
           if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 2))) break;
-          mbar_arrive_expect_tx(&full[s], tx);
+          if (leader) mbar_arrive_expect_tx(&full[s], mult * tx);
           const int kx = FP4 ? kt * kRowBytes : kt * 64;
-          tma_load_2d(smem + C::offA + s * C::kA, &tmA, &full[s], kx, m0);
-          tma_load_2d(smem + C::offB + s * C::kB, &tmB, &full[s], kx, n0);
-          if (FP4) {
-            bulk_load(smem + C::offSFA + s * C::kSFA, p.a_sf + ((int64_t)m_blk * kchunks + kt * 4) * 512, 2048,
-                      &full[s]);
-            for (int h = 0; h < sfb_halves; ++h)
-              bulk_load(smem + C::offSFB + s * C::kSFB + h * 2048,
-                        p.w_sf + ((int64_t)(n_blk * ((BN + 127) / 128) + h) * kchunks + kt * 4) * 512, 2048,
+          if (PAIR) {
+            tma_load_2d_pair(smem + C::offA + s * C::kA, &tmA, &full[s], kx, am0);
+            tma_load_2d_pair(smem + C::offB + s * C::kB, &tmB, &full[s], kx, bn0);
+            if (FP4) {  // scale chunks through 256-byte-row views of the scale buffers (2 KB boxes)
+              tma_load_2d_pair(smem + C::offSFA + s * C::kSFA, &tmSFA, &full[s], 0,
+                               (int)(((int64_t)(am0 / kBM) * kchunks + kt * 4) * 2));
+              for (int h = 0; h < sfb_halves; ++h)
+                tma_load_2d_pair(smem + C::offSFB + s * C::kSFB + h * 2048, &tmSFB, &full[s], 0,
+                                 (int)(((int64_t)(n0 / 128 + h) * kchunks + kt * 4) * 2));
+            }
+          } else {
+            tma_load_2d(smem + C::offA + s * C::kA, &tmA, &full[s], kx, am0);
+            tma_load_2d(smem + C::offB + s * C::kB, &tmB, &full[s], kx, bn0);
+            if (FP4) {
+              bulk_load(smem + C::offSFA + s * C::kSFA, p.a_sf + ((int64_t)m_blk * kchunks + kt * 4) * 512, 2048,
                         &full[s]);
+              for (int h = 0; h < sfb_halves; ++h)
+                bulk_load(smem + C::offSFB + s * C::kSFB + h * 2048,
+                          p.w_sf + ((int64_t)(n_blk * ((BN + 127) / 128) + h) * kchunks + kt * 4) * 512, 2048,
+                          &full[s]);
+            }
           }
         }
       }
-      // drain: never leave the CTA with copies in flight (returns at once on the normal path)
+      // drain: never leave the CTA with copies in flight (returns at once on the normal path);
+      // a pair's copies all complete on the leader's barriers, which the leader drains
+      if (!leader) g = 0;
       for (uint32_t i = g > (uint32_t)STAGES ? g - STAGES : 0; i < g; ++i) {
         volatile int never = 0;
         mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never, globaltimer(), p.status, 3);
@@ -212,13 +255,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      const uint32_t idesc = FP4 ? idesc_mxf4nvf4(kBM, BN) : idesc_bf16(kBM, BN);
-      const uint32_t ib = idesc_bf16(kBM, BN);
+    // ------------------------------------------------------------ MMA issuer (pair leader)
+    if (elect_one() && leader) {
+      const uint32_t idesc = FP4 ? idesc_mxf4nvf4(kTileM, BN) : idesc_bf16(kTileM, BN);
+      const uint32_t ib = idesc_bf16(kTileM, BN);
       uint32_t g = 0, it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
+      for (int tile = cid; ok && tile < num_tiles; tile += ncl, ++it) {
         // the epilogue must have drained the previous tile's accumulator
         if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4))) break;
         tc_fence_after();
@@ -231,11 +274,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t lb = sw128_desc(smem + C::offB + s * C::kB);
           for (int j = 0; j < 4; ++j) {
             if (b * 64 + j * 16 < p.lora_rank) {
-              mma_bf16(tmem, la + 2 * j, lb + 2 * j, ib, accum);
+              if (PAIR)
+                mma_bf16_pair(tmem, la + 2 * j, lb + 2 * j, ib, accum);
+              else
+                mma_bf16(tmem, la + 2 * j, lb + 2 * j, ib, accum);
               accum = 1;
             }
           }
-          tc_commit(&empty[s]);
+          if (PAIR)
+            tc_commit_pair(&empty[s]);
+          else
+            tc_commit(&empty[s]);
         }
         for (int kt = 0; ok && kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
@@ -248,32 +297,64 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint8_t* sfb = smem + C::offSFB + s * C::kSFB;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              tc_cp_32x128b_warpx4(tmem + C::kSfaCol + 4 * j, sf_desc(sfa + j * 512));
+              // a pair copies each CTA's scale chunks (same offsets) into its own TMEM
+              if (PAIR)
+                tc_cp_32x128b_warpx4_pair(tmem + C::kSfaCol + 4 * j, sf_desc(sfa + j * 512));
+              else
+                tc_cp_32x128b_warpx4(tmem + C::kSfaCol + 4 * j, sf_desc(sfa + j * 512));
 #pragma unroll
-              for (int h = 0; h < (BN + 127) / 128; ++h)
-                tc_cp_32x128b_warpx4(tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j + 4 * h,
-                                     sf_desc(sfb + h * 2048 + j * 512));
+              for (int h = 0; h < (BN + 127) / 128; ++h) {
+                if (PAIR)
+                  tc_cp_32x128b_warpx4_pair(tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j + 4 * h,
+                                            sf_desc(sfb + h * 2048 + j * 512));
+                else
+                  tc_cp_32x128b_warpx4(tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j + 4 * h,
+                                       sf_desc(sfb + h * 2048 + j * 512));
+              }
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              mma_mxf4nvf4(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + C::kSfaCol + 4 * j,
-                           tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j, accum);
+              if (PAIR)
+                mma_mxf4nvf4_pair(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + C::kSfaCol + 4 * j,
+                                  tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j, accum);
+              else
+                mma_mxf4nvf4(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + C::kSfaCol + 4 * j,
+                             tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j, accum);
               accum = 1;
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              mma_bf16(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, accum);
+              if (PAIR)
+                mma_bf16_pair(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, accum);
+              else
+                mma_bf16(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, accum);
               accum = 1;
             }
           }
-          tc_commit(&empty[s]);
+          if (PAIR)
+            tc_commit_pair(&empty[s]);
+          else
+            tc_commit(&empty[s]);
         }
-        tc_commit(acc_full);
+        if (PAIR)
+          tc_commit_pair(acc_full);
+        else
+          tc_commit(acc_full);
       }
-      if (!ok) tc_commit(acc_full);  // wake the epilogue on the abort path
-      // every MMA of this CTA has completed before anyone frees TMEM
-      tc_commit(mma_done);
+      if (!ok) {  // wake the epilogue on the abort path
+        if (PAIR)
+          tc_commit_pair(acc_full);
+        else
+          tc_commit(acc_full);
+      }
+      // every MMA has completed before anyone frees TMEM
+      if (PAIR)
+        tc_commit_pair(mma_done);
+      else
+        tc_commit(mma_done);
+    }
+    if (lane == 0) {  // both CTAs of a pair learn of the last MMA through their own barrier
       volatile int never = 0;
       mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9);
     }
@@ -288,9 +369,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t hnv = smem_u32(smem + C::offHn) + ew * (C::kColsPerWarp * 4);
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     uint32_t it = 0, nstore = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    for (int tile = cid; tile < num_tiles; tile += ncl, ++it) {
       const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
-      const int m0 = m_blk * kBM, n0 = n_blk * BN;
+      const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;  // this CTA's 128 rows
       const int ncol0 = n0 + half * C::kColsPerWarp;
       // Everything that does not depend on the accumulator is fetched while the MMAs run:
       // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
@@ -333,7 +414,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);  // TMEM drained: the next tile's MMAs may start
+      if (lane == 0) {  // TMEM drained: the next tile's MMAs may start (the leader counts both CTAs)
+        if (PAIR && !leader)
+          mbar_arrive_cluster(acc_empty, 0);
+        else
+          mbar_arrive(acc_empty);
+      }
 
       // row domain, one row per lane: y = bf16(alpha * acc + bias) (FP4), bf16(acc * col_scale / alpha)
       // (LoRA down-projection) or bf16(acc + bias) (plain bf16 linear: no column scale)
@@ -478,18 +564,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // no CTA of a pair leaves while the other may still touch its memory
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, C::kTmemCols);
+    else
+      tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
-template <int BN, int STAGES, bool FP4>
+template <int BN, int STAGES, bool FP4, bool PAIR = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
-                const CUtensorMap& o, GemmParams p, cudaStream_t st) {
-  using C = GemmCfg<BN, STAGES, FP4>;
-  auto kern = gemm_kernel<BN, STAGES, FP4>;
+                const CUtensorMap& o, GemmParams p, cudaStream_t st, const CUtensorMap* sfa = nullptr,
+                const CUtensorMap* sfb = nullptr) {
+  using C = GemmCfg<BN, STAGES, FP4, PAIR>;
+  auto kern = gemm_kernel<BN, STAGES, FP4, PAIR>;
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {
     DEMON_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
@@ -498,15 +591,47 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   int dev = 0, sms = 148;
   DEMON_CUDA(cudaGetDevice(&dev));
   DEMON_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  p.m_tiles = (p.M + kBM - 1) / kBM;
+  constexpr int tile_m = PAIR ? 2 * kBM : kBM;
+  p.m_tiles = (p.M + tile_m - 1) / tile_m;
   p.n_tiles = (p.N + BN - 1) / BN;
   const int tiles = p.m_tiles * p.n_tiles;
-  const dim3 grid((unsigned)std::min(tiles, sms));
-  kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, o, p);
-  DEMON_CUDA(cudaGetLastError());
+  CUtensorMap z;
+  memset(&z, 0, sizeof z);
+  if (!PAIR) {
+    const dim3 grid((unsigned)std::min(tiles, sms));
+    kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, o, z, z, p);
+    DEMON_CUDA(cudaGetLastError());
+    return DEMON_OK;
+  }
+  // persistent CTA pairs: one pair per two SMs, clusters of 2
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * std::min(tiles, sms / 2)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DEMON_CUDA(cudaLaunchKernelEx(&cfg, kern, a, b, la, lb, o, sfa ? *sfa : z, sfb ? *sfb : z, p));
   return DEMON_OK;
 }
 
+}  // namespace demon
+
+namespace demon {
+// CTA-pair tiles are the default for N % 256 == 0; DEMON_GEMM_PAIR=0 selects the one-CTA
+// kernel (kept for comparison and as the N % 256 != 0 path).
+static bool pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("DEMON_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 }  // namespace demon
 
 using namespace demon;
@@ -563,8 +688,20 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   memset(&tlb, 0, sizeof tlb);
   DEMON_RC(make_tmap_2d(&ta, a->a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)M,
                         (uint64_t)K / 2, 128, 128));
+  // N % 256 == 0: 256 x 256 tiles on CTA pairs (each CTA loads half of the B tile)
+  const bool pair = bn256 && pair_gemm_enabled();
   DEMON_RC(make_tmap_2d(&tb, a->w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K / 2, (uint64_t)N,
-                        (uint64_t)K / 2, 128, BN));
+                        (uint64_t)K / 2, 128, pair ? BN / 2 : BN));
+  // scale buffers as rows of 256 bytes: one 2 KB box is one stage's 128-row scale chunk run
+  CUtensorMap tsfa, tsfb;
+  memset(&tsfa, 0, sizeof tsfa);
+  memset(&tsfb, 0, sizeof tsfb);
+  if (pair) {
+    DEMON_RC(make_tmap_2d(&tsfa, a->a_sf, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256,
+                          (uint64_t)(((M + 127) / 128) * K / 32), 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE));
+    DEMON_RC(make_tmap_2d(&tsfb, a->w_sf, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256,
+                          (uint64_t)(((N + 127) / 128) * K / 32), 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
   // output: 32 x 32 bf16 store boxes (64-byte rows, 64-byte swizzle); rows past M are clipped
   CUtensorMap to;
   DEMON_RC(make_tmap_2d(&to, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
@@ -572,7 +709,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   if (lora) {
     const uint64_t r = (uint64_t)a->lora_rank;
     DEMON_RC(make_tmap_2d(&tla, a->lora_xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)M, r * 2, 64, 128));
-    DEMON_RC(make_tmap_2d(&tlb, a->lora_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)N, r * 2, 64, BN));
+    DEMON_RC(make_tmap_2d(&tlb, a->lora_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, r, (uint64_t)N, r * 2, 64,
+                          pair ? BN / 2 : BN));
   }
   GemmParams p{};
   p.a_sf = a->a_sf;
@@ -603,6 +741,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.hn_eps = a->hn_eps;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
   return launch_gemm<128, 5, true>(ta, tb, tla, tlb, to, p, st);
 }
