@@ -36,6 +36,7 @@ from dataclasses import dataclass
 
 import torch
 from torch import nn
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import nvfp4 as Q
 from .nvfp4 import NVFP4Linear
@@ -86,11 +87,22 @@ class RMSNorm(nn.Module):
 
 def _attention(q, k, v, window: int | None):
     """softmax(q k^T / sqrt(128)) v, GQA, optional bidirectional band |i - j| <= window.
-    q [B, S, Hq, 128], k / v [B, L, Hk, 128] (strided views are fine)."""
+    q [B, S, Hq, 128], k / v [B, L, Hk, 128] (strided views are fine); returns [B, S, Hq, 128].
+
+    Library kernels, both computing each (sequence, head, query tile) from that sequence alone
+    (no split over the keys), so results do not depend on the batch: full attention (global
+    self-attention layers, cross-attention) runs cuDNN's fused attention through PyTorch SDPA;
+    the sliding-window layers run FlashAttention-2 with its local window (block-skipping)
+    and an unsplit KV loop.
+    """
+    if window is None:
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), enable_gqa=True)
+        return o.transpose(1, 2)
     if _fa_kvcache is None:
-        raise RuntimeError(f"flash_attn is required for the DiT attention: {_fa_error!r}")
-    ws = (-1, -1) if window is None else (window, window)
-    return _fa_kvcache(q, k, v, window_size=ws, num_splits=1)
+        raise RuntimeError(f"flash_attn is required for the DiT sliding-window attention: {_fa_error!r}")
+    return _fa_kvcache(q, k, v, window_size=(window, window), num_splits=1)
 
 
 class TimestepEmbedding(nn.Module):

@@ -109,3 +109,30 @@ def test_dit_nvfp4_forward_matches_reference_fake_quant(cuda):
     d1 = {k: (v[:1] if isinstance(v, torch.Tensor) and v.dim() > 0 else v) for k, v in d.items()}
     out1 = _run(m, d1, cuda)
     assert torch.equal(out1, out[:1])
+
+
+@pytest.mark.gpu
+def test_attention_batch_invariant_at_dit_shapes(cuda):
+    """The DiT attention (cuDNN full / cross, FlashAttention-2 window) computes a sequence from
+    that sequence alone at the DiT's shapes (750 tokens, GQA 16/8, text 256)."""
+    from demon_b200.dit import _attention
+    g = torch.Generator(device=cuda).manual_seed(0)
+    B, S, L = 6, 750, 256
+    q = torch.randn(B, S, 16, 128, generator=g, device=cuda).to(torch.bfloat16)
+    k = torch.randn(B, S, 8, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, S, 8, 128, generator=g, device=cuda).to(torch.bfloat16)
+    ke = torch.randn(B, L, 8, 128, generator=g, device=cuda).to(torch.bfloat16)
+    ve = torch.randn(B, L, 8, 128, generator=g, device=cuda).to(torch.bfloat16)
+    for kk, vv, w in ((k, v, None), (k, v, 128), (ke, ve, None)):
+        full = _attention(q, kk, vv, w)
+        for b in (0, B - 1):
+            one = _attention(q[b:b + 1], kk[b:b + 1], vv[b:b + 1], w)
+            assert torch.equal(one[0], full[b]), (w, b)
+        # against fp32 math
+        i = torch.arange(S, device=cuda)
+        Lk = kk.shape[1]
+        mask = None if w is None else ((i[:, None] - torch.arange(Lk, device=cuda)[None, :]).abs() <= w)
+        ref = torch.nn.functional.scaled_dot_product_attention(
+            q[:2].transpose(1, 2).float(), kk[:2].transpose(1, 2).float(), vv[:2].transpose(1, 2).float(),
+            attn_mask=mask, enable_gqa=True).transpose(1, 2)
+        assert _rel(full[:2], ref) < 1e-2
