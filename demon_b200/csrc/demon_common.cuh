@@ -404,5 +404,11 @@ __device__ __forceinline__ uint32_t mul_bf2(uint32_t a, uint32_t b) {
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// bf16(a + b) per half (single rounding of the exact sum; equal to the fp32 sum rounded to bf16).
+__device__ __forceinline__ uint32_t add_bf2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 
 }  // namespace demon

@@ -39,38 +39,37 @@ struct NormArgs {
   int64_t ldy;
 };
 
-// Eight bf16 (x) -> bf16(bf16(bf16(w * bf16(x * rinv)) * s1) + sh) (products / sum skipped
-// when s1 / sh are absent), as Qwen3RMSNorm followed by the AdaLN modulation.
+// Eight bf16 (x) -> bf16(bf16(bf16(w * bf16(x * rinv)) * s1) + sh) (product / sum skipped when
+// s1 / sh are absent), as Qwen3RMSNorm followed by the AdaLN modulation, in packed arithmetic:
+// x * rinv in fp32 then rounded; the products and the sum of two bf16 operands by the bf16x2
+// instructions, whose single rounding of the exact result equals the reference's fp32
+// operation followed by rounding to bf16 (the fp32 result is exact, or the smaller operand is
+// far below half an ulp of the larger).
 template <bool MUL, bool ADD>
 __device__ __forceinline__ uint4 norm8(uint4 x, uint4 w, uint4 s1, uint4 sh, float rinv) {
   const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, ww[4] = {w.x, w.y, w.z, w.w};
   const uint32_t sw[4] = {s1.x, s1.y, s1.z, s1.w}, hw[4] = {sh.x, sh.y, sh.z, sh.w};
+  const float2 r2 = make_float2(rinv, rinv);
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float lo = bf16r(__fmul_rn(bf16_lo(ww[i]), bf16r(__fmul_rn(bf16_lo(xw[i]), rinv))));
-    float hi = bf16r(__fmul_rn(bf16_hi(ww[i]), bf16r(__fmul_rn(bf16_hi(xw[i]), rinv))));
-    if (MUL) {
-      lo = bf16r(__fmul_rn(lo, bf16_lo(sw[i])));
-      hi = bf16r(__fmul_rn(hi, bf16_hi(sw[i])));
-    }
-    if (ADD) {
-      lo = bf16r(__fadd_rn(lo, bf16_lo(hw[i])));
-      hi = bf16r(__fadd_rn(hi, bf16_hi(hw[i])));
-    }
-    o[i] = pack_bf16(lo, hi);
+    uint32_t v = mul_bf2(ww[i], f2_bf2(mul_f2(bf2_f2(xw[i]), r2)));
+    if (MUL) v = mul_bf2(v, sw[i]);
+    if (ADD) v = add_bf2(v, hw[i]);
+    o[i] = v;
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __device__ __forceinline__ float sumsq8(uint4 v, float acc) {
   const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+  float2 s = make_float2(acc, 0.0f);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    acc = __fadd_rn(acc, __fmul_rn(bf16_lo(w4[i]), bf16_lo(w4[i])));
-    acc = __fadd_rn(acc, __fmul_rn(bf16_hi(w4[i]), bf16_hi(w4[i])));
+    const float2 f = bf2_f2(w4[i]);
+    s = fma_f2(f, f, s);
   }
-  return acc;
+  return s.x + s.y;
 }
 
 // y = ((w * bf16(x * rsqrt(mean(x^2) + eps))) * (1 + scale)) + shift, each product / sum
@@ -115,7 +114,7 @@ __global__ void __launch_bounds__(256) adanorm_quant_kernel(const NormArgs a) {
 #pragma unroll
   for (int j = 0; j < 2 * G::NB; ++j) {
     xv[j] = norm8<MUL, ADD>(xv[j], wv[j], sv[j], hv[j], rinv);
-    am = fmaxf(am, amax8(xv[j]));
+    am = fmaxf(am, absmax8_fast(xv[j]));
   }
   if (a.y && live) {
     uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
@@ -154,17 +153,25 @@ struct SiluArgs {
   uint8_t* sf;
 };
 
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint4 silu_mul8(uint4 g, uint4 u) {
   const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float g0 = bf16_lo(gw[i]), g1 = bf16_hi(gw[i]);
-    // silu(g) = g / (1 + exp(-g)) with the hardware exp / divide approximations: the result is
-    // rounded to bf16 (8 mantissa bits), far coarser than their error
-    const float s0 = bf16r(__fdividef(g0, 1.0f + __expf(-g0)));
-    const float s1 = bf16r(__fdividef(g1, 1.0f + __expf(-g1)));
-    o[i] = pack_bf16(__fmul_rn(s0, bf16_lo(uw[i])), __fmul_rn(s1, bf16_hi(uw[i])));
+    // silu(g) = g * sigmoid(g) = g * (1/2 + tanh(g/2) / 2), one hardware tanh per element; the
+    // result is rounded to bf16 (8 significant bits), coarser than the approximation's error,
+    // then multiplied by up in bf16 (exact product, one rounding)
+    const float2 gf = bf2_f2(gw[i]);
+    const float2 hf = make_float2(0.5f * gf.x, 0.5f * gf.y);
+    const float2 th = make_float2(tanh_approx(hf.x), tanh_approx(hf.y));
+    const float2 sf = fma_f2(hf, th, hf);  // g/2 + g/2 * tanh(g/2)
+    o[i] = mul_bf2(f2_bf2(sf), uw[i]);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -198,7 +205,7 @@ __global__ void __launch_bounds__(256) silu_mul_quant_kernel(const SiluArgs a) {
 #pragma unroll
   for (int j = 0; j < 2 * G::NB; ++j) {
     gv[j] = silu_mul8(gv[j], uv[j]);
-    am = fmaxf(am, amax8(gv[j]));
+    am = fmaxf(am, absmax8_fast(gv[j]));
   }
   am = row_reduce<G::W, true>(am, red, warp, lane);
   if (m >= a.Mpad) return;

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(256) quantize_blocks_kernel(const __nv_bfloat1
   } else {
     float am = 0.0f;
 #pragma unroll
-    for (int j = 0; j < G::NB; ++j) am = fmaxf(am, fmaxf(amax8(a[j]), amax8(b[j])));
+    for (int j = 0; j < G::NB; ++j) am = fmaxf(am, fmaxf(absmax8_fast(a[j]), absmax8_fast(b[j])));
     g = global_scale(row_reduce<G::W, true>(am, red, warp, lane));
     if (wr == 0 && lane == 0 && !pad) gs[m] = g;
   }

@@ -111,8 +111,35 @@ struct QBlock {
   uint2 codes;
   uint32_t sb;
 };
+// Eight elements -> 32 bits of codes, for blocks known to hold no NaN (no per-element
+// NaN test; otherwise identical to pack8).
+__device__ __forceinline__ uint32_t pack2_finite(uint32_t w, float rs) {
+  const float2 p = mul2(make_float2(bf16_lo(w), bf16_hi(w)), rs);
+  return (uint32_t)__nv_cvt_float2_to_fp4x2(p, __NV_E2M1, cudaRoundNearest);
+}
+__device__ __forceinline__ uint32_t pack8_finite(uint4 v, float rs) {
+  const uint32_t c = pack2_finite(v.x, rs) | (pack2_finite(v.y, rs) << 8) | (pack2_finite(v.z, rs) << 16) |
+                     (pack2_finite(v.w, rs) << 24);
+  const uint32_t mag = c & 0x77777777u;
+  const uint32_t nz = (mag | (mag >> 1) | (mag >> 2)) & 0x11111111u;
+  return mag | (c & (nz << 3));
+}
+
+// Largest |x| bit pattern of 16 bf16 values, per half-word: for non-negative IEEE values the
+// bit patterns order like the values, so an unsigned SIMD max gives the absmax exactly;
+// a result above 0x7F80 (infinity) means the block holds a NaN.
+__device__ __forceinline__ uint32_t absmax_bits16(uint4 a, uint4 b) {
+  const uint32_t k = 0x7FFF7FFFu;
+  const uint32_t m = __vmaxu2(__vmaxu2(__vmaxu2(a.x & k, a.y & k), __vmaxu2(a.z & k, a.w & k)),
+                              __vmaxu2(__vmaxu2(b.x & k, b.y & k), __vmaxu2(b.z & k, b.w & k)));
+  return max(m & 0xFFFFu, m >> 16);
+}
+
 __device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float denom) {
-  const float am = fmaxf(amax8(a), amax8(b));
+  const uint32_t mb = absmax_bits16(a, b);
+  const bool nan = mb > 0x7F80u;
+  // NaN elements do not count towards the block absmax (the packed max ignores them)
+  const float am = nan ? fmaxf(amax8(a), amax8(b)) : __uint_as_float(mb << 16);
   const float s = fminf(__fdiv_rn(am, denom), 448.0f);
   QBlock q;
   q.sb = e4m3_rne_sat(s);
@@ -120,9 +147,17 @@ __device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float d
   const float sbf = e4m3_to_f32(q.sb);
   if (sbf != 0.0f) {
     const float rs = __frcp_rn(__fmul_rn(sbf, g));
-    q.codes = make_uint2(pack8(a, rs), pack8(b, rs));
+    q.codes = nan ? make_uint2(pack8(a, rs), pack8(b, rs)) : make_uint2(pack8_finite(a, rs), pack8_finite(b, rs));
   }
   return q;
+}
+
+// Row absmax of finite-or-NaN bf16 data (NaN ignored, as the packed max does): amax of 8 values.
+__device__ __forceinline__ float absmax8_fast(uint4 v) {
+  const uint32_t k = 0x7FFF7FFFu;
+  uint32_t m = __vmaxu2(__vmaxu2(v.x & k, v.y & k), __vmaxu2(v.z & k, v.w & k));
+  m = max(m & 0xFFFFu, m >> 16);
+  return m > 0x7F80u ? amax8(v) : __uint_as_float(m << 16);
 }
 
 // Lane owns scale block kb of row m (K/16 blocks per row): store its 8 code bytes and, from

@@ -226,6 +226,8 @@ class StreamPipeline:
         self.ticks = 0
         self._last_tick_ms = 0.0
         self._gain_dirty = False
+        self._stage = [(None, None)] * 16   # pinned noise staging ring
+        self._stage_i = 0
 
     # ------------------------------------------------------------------ properties
     @property
@@ -325,7 +327,20 @@ class StreamPipeline:
             if seed is not None:
                 torch.manual_seed(int(seed))
             n = torch.randn(1, D, T, dtype=torch.float32)
-        return n.movedim(-1, -2)[0].to(device=self._device, dtype=self._dtype).contiguous()
+        host = n.movedim(-1, -2)[0].to(self._dtype).contiguous()   # bf16 rounding as .to(dtype) does
+        # upload through a ring of pinned buffers (a pageable copy would stall the host on the GPU)
+        k = self._stage_i = (self._stage_i + 1) % len(self._stage)
+        buf, ev = self._stage[k]
+        if buf is None or buf.shape != host.shape:
+            buf = torch.empty(host.shape, dtype=host.dtype).pin_memory()
+        elif ev is not None:
+            ev.synchronize()        # the copy that last read this buffer has finished
+        buf.copy_(host)
+        out = buf.to(self._device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self._device))
+        self._stage[k] = (buf, ev)
+        return out
 
     def _ensure_buffers(self, T: int) -> None:
         if self._T != T or self._dec is None or self._dec.shape[0] != self._depth:
