@@ -87,88 +87,87 @@ __device__ __forceinline__ void philox_normal4(uint64_t seed, uint64_t step, uin
   for (int i = 0; i < 2; ++i) {
     const float u1 = __uint2float_rn(u[2 * i] >> 8) * 5.9604644775390625e-08f + 2.98023223876953125e-08f;
     const float u2 = __uint2float_rn(u[2 * i + 1] >> 8) * 5.9604644775390625e-08f;
-    const float r = sqrtf(-2.0f * logf(u1));
+    // hardware log / sqrt / sin / cos approximations: the draws are rounded to bf16 (8
+    // significant bits), far coarser than their error
+    const float r = __fsqrt_rn(-2.0f * __logf(u1));
     float s, c;
-    sincospif(2.0f * u2, &s, &c);
+    __sincosf(6.2831853071795865f * (u2 - 0.5f), &s, &c);  // a uniform angle in [-pi, pi)
     z[2 * i] = rnd(r * c);
     z[2 * i + 1] = rnd(r * s);
   }
 }
 
 struct OdeShared {
-  float warp_part[kOdeThreads / 32][16][32];  // per-warp moment partials
-  double cta_part[kOdeD][8];                   // this CTA's moments (read by the cluster)
+  float gpart[4][kOdeD][8];     // per row-group moment partials (fp32 over the group's rows)
+  double cta_part[kOdeD][8];    // this CTA's moments (read by the cluster)
   float k[kOdeD], a[kOdeD], sigma[kOdeD];
 };
 
-// Velocity blend over active conditions (ode_steps.py:150-183); one condition
+// ---------------------------------------------------------------------------
+// Packed arithmetic on pairs of channels.  A bf16x2 product or sum of two bf16 operands
+// (mul_bf2 / add_bf2 / sub_bf2) rounds the exact result once, which equals the reference's
+// fp32 operation followed by rounding to bf16; an fp32 scalar times a bf16 tensor goes
+// through fp32 (mul_f2) and is rounded afterwards (f2_bf2), as torch's opmath does.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sub_bf2(uint32_t a, uint32_t b) { return add_bf2(a, b ^ 0x80008000u); }
+__device__ __forceinline__ uint32_t bf2_dup(float v) { return pack_bf16x2(v, v); }  // v already bf16-exact
+__device__ __forceinline__ float2 f2_dup(float v) { return make_float2(v, v); }
+// bf16(s * x) for an fp32 scalar s and a bf16 pair x
+__device__ __forceinline__ uint32_t scal_bf2(float s, uint32_t x) { return f2_bf2(mul_f2(f2_dup(s), bf2_f2(x))); }
+
+// mask_pre_blend (ode_steps.py:89-106): m x + (1 - m)(t noise + (1 - t) orig), each product and
+// sum rounded to bf16 as the reference's eager tensors are.  m2 / om2 = bf16 pairs of m, 1 - m.
+__device__ __forceinline__ uint32_t pre_blend2(uint32_t x, uint32_t nz, uint32_t o, uint32_t m2, uint32_t om2,
+                                               float t) {
+  const uint32_t noised = add_bf2(scal_bf2(t, nz), scal_bf2(1.0f - t, o));
+  return add_bf2(mul_bf2(m2, x), mul_bf2(om2, noised));
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p, int64_t off) {
+  return __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + off));
+}
+__device__ __forceinline__ void stg16(void* p, int64_t off, uint4 v) {
+  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p) + off) = v;
+}
+__device__ __forceinline__ void sts16(__nv_bfloat16* base, int64_t off, uint4 v) {
+  st_shared_v4(smem_u32(base + off), v.x, v.y, v.z, v.w);
+}
+__device__ __forceinline__ uint4 lds16(const __nv_bfloat16* base, int64_t off) { return ld_shared_v4(smem_u32(base + off)); }
+
+// Velocity blend over active conditions (ode_steps.py:150-183), 8 channels; one condition
 // means no blend (stream.py:1068-1069).
-__device__ __forceinline__ void blend(const void* const* v, const float* const* w, int n, int64_t off, int t,
-                                      float (&out)[4]) {
-  if (n <= 1) {
-    ld4(v[0], off, out);
-    return;
-  }
-  float num[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
+__device__ __forceinline__ uint4 blend8(const void* const* v, const float* const* w, int n, int64_t off, int t) {
+  if (n <= 1) return ldg16(v[0], off);
+  float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, den = 0.f;
   for (int i = 0; i < n && i < DEMON_ODE_MAX_COND; ++i) {
-    float x[4];
-    ld4(v[i], off, x);
+    const uint4 x = ldg16(v[i], off);
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
     const float wi = w[i] ? __ldg(w[i] + t) : 1.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) num[j] = fmaf(x[j], wi, num[j]);
+    for (int j = 0; j < 4; ++j) {
+      num[2 * j] = fmaf(bf16_lo(xw[j]), wi, num[2 * j]);
+      num[2 * j + 1] = fmaf(bf16_hi(xw[j]), wi, num[2 * j + 1]);
+    }
     den += wi;
   }
   const float dd = fmaxf(den, 1e-8f);
+  uint32_t o[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) out[j] = rnd(__fdiv_rn(num[j], dd));
+  for (int j = 0; j < 4; ++j) o[j] = pack_bf16x2(__fdiv_rn(num[2 * j], dd), __fdiv_rn(num[2 * j + 1], dd));
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// mask_pre_blend (ode_steps.py:89-106): m x + (1 - m)(t noise + (1 - t) orig),
-// rounded after every operation as the reference's eager bf16 tensors are
-// (the products and sums of bf16 operands are exact in fp32, so this is bit-exact).
-__device__ __forceinline__ void pre_blend(const DemonOdeSlot& S, int64_t off, float m, float t, float (&x)[4]) {
-  float o[4], nz[4];
-  ld4(S.mask_orig, off, o);
-  ld4(S.mask_noise, off, nz);
-  const float om = rnd(1.0f - m), ot = 1.0f - t;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float noised = rnd(rnd(t * nz[j]) + rnd(ot * o[j]));
-    x[j] = rnd(rnd(m * x[j]) + rnd(om * noised));
-  }
+__device__ __forceinline__ void words(uint4 v, uint32_t (&w)[4]) {
+  w[0] = v.x;
+  w[1] = v.y;
+  w[2] = v.z;
+  w[3] = v.w;
 }
 
-// (1 - c) x + c y, op by op (mask_post_blend_x0 / blend_x0_target, ode_steps.py:109-142)
-__device__ __forceinline__ float lerp_eager(float x, float c, float y) {
-  return rnd(rnd(rnd(1.0f - c) * x) + rnd(c * y));
-}
-
-__device__ __forceinline__ void write_dec(const DemonOdeSlot& S, const __nv_bfloat16* gain, int64_t off, int t,
-                                          bool masked, float m, float tn, float (&x)[4]) {
-  float d[4] = {x[0], x[1], x[2], x[3]};
-  if (masked) pre_blend(S, off, m, tn, d);
-  if (gain) {
-    float g[4];
-    ld4(gain, off, g);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) d[j] = d[j] * g[j];
-  }
-  st4(S.dec_out, off, d);
-}
-
-__device__ __forceinline__ void unpack4(uint2 u, float (&v)[4]) {
-  v[0] = bf16_lo(u.x);
-  v[1] = bf16_hi(u.x);
-  v[2] = bf16_lo(u.y);
-  v[3] = bf16_hi(u.y);
-}
-__device__ __forceinline__ uint2 ldraw(const void* p, int64_t off) {
-  return *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + off);
-}
-
-constexpr int kRB = 4;  // rows per batch and thread: all loads of a batch are issued before its compute
-
-__global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
+// Layout: a slot's T rows are split over an 8-CTA cluster.  Row passes: thread = (row r in
+// [0, 32), channel octet q in [0, 8)) with 16-byte loads; the moment pass: thread = (channel c,
+// row group g in [0, 4)) over the rows staged in shared memory.
+__global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
                                                                const __nv_bfloat16* __restrict__ gain,
                                                                int prepare_only) {
   extern __shared__ __align__(16) uint8_t ode_smem[];
@@ -181,9 +180,9 @@ __global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOde
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int slot_id = blockIdx.x / kOdeCluster;
-  const int tid = threadIdx.x, cgp = tid & 15, rg = tid >> 4;
-  // the slot descriptor, once per CTA, into shared memory
-  {
+  const int tid = threadIdx.x;
+  const int rr = tid >> 3, c0 = (tid & 7) * 8;  // row in pass, first channel of the octet
+  {  // the slot descriptor, once per CTA, into shared memory
     const uint64_t* src = reinterpret_cast<const uint64_t*>(slots + slot_id);
     uint64_t* dst = reinterpret_cast<uint64_t*>(&s_slot);
     for (int i = tid; i < (int)(sizeof(DemonOdeSlot) / 8); i += kOdeThreads) dst[i] = __ldg(src + i);
@@ -192,16 +191,28 @@ __global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOde
   const DemonOdeSlot& S = s_slot;
   const int flags = S.flags;
   const int t0 = crank * Tc, t1 = min(T, t0 + Tc);
-  const int c0 = cgp * 4;
 
-  if (prepare_only) {
+  if (prepare_only) {  // decoder input at the current step: mask pre-blend at t_curr, times the gain
     if (!(flags & DEMON_ODE_DEC_OUT)) return;
-    for (int t = t0 + rg; t < t1; t += 16) {
+    const bool dm = (flags & DEMON_ODE_DEC_MASK) != 0;
+    for (int t = t0 + rr; t < t1; t += 32) {
       const int64_t off = (int64_t)t * kOdeD + c0;
-      float x[4];
-      ld4(S.xt, off, x);
-      const float m = (flags & DEMON_ODE_DEC_MASK) ? rnd(__ldg(S.mask + t) * S.mask_s) : 0.f;
-      write_dec(S, gain, off, t, (flags & DEMON_ODE_DEC_MASK) != 0, m, S.t_curr, x);
+      uint32_t x[4], o[4], nz[4], g[4];
+      words(ldg16(S.xt, off), x);
+      if (dm) {
+        words(ldg16(S.mask_orig, off), o);
+        words(ldg16(S.mask_noise, off), nz);
+        const float m = rnd(__ldg(S.mask + t) * S.mask_s);
+        const uint32_t m2 = bf2_dup(m), om2 = bf2_dup(rnd(1.0f - m));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = pre_blend2(x[j], nz[j], o[j], m2, om2, S.t_curr);
+      }
+      if (gain) {
+        words(ldg16(gain, off), g);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = mul_bf2(x[j], g[j]);
+      }
+      stg16(S.dec_out, off, make_uint4(x[0], x[1], x[2], x[3]));
     }
     return;
   }
@@ -211,80 +222,82 @@ __global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOde
   const bool cache_neg = (flags & DEMON_ODE_CACHE_NEG) != 0;
   const int n_pos = S.n_pos, n_neg = S.n_neg;
 
-  // ---------------- phase 1: velocity assembly, momentum, moments ----------
-  float mom[8][4];
+  // ---------------- phase 1: velocity assembly and momentum, staged in shared memory -------
+  for (int tb = t0 + rr; tb < t1; tb += 64) {
+    const int tA = tb, tB = tb + 32;  // two rows per thread in flight
+    const bool hasB = tB < t1;
+    const int64_t offA = (int64_t)tA * kOdeD + c0, offB = (int64_t)(hasB ? tB : tA) * kOdeD + c0;
+    const uint4 vpA = blend8(S.v_pos, S.w_pos, n_pos, offA, tA);
+    const uint4 vpB = blend8(S.v_pos, S.w_pos, n_pos, offB, hasB ? tB : tA);
+    sts16(vp_s, (int64_t)(tA - t0) * kOdeD + c0, vpA);
+    if (hasB) sts16(vp_s, (int64_t)(tB - t0) * kOdeD + c0, vpB);
+    if (cfg) {
+      const uint4 vnA = blend8(S.v_neg, S.w_neg, n_neg, offA, tA);
+      const uint4 vnB = blend8(S.v_neg, S.w_neg, n_neg, offB, hasB ? tB : tA);
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      const uint4 moA = mom_init ? z : ldg16(S.momentum, offA);
+      const uint4 moB = mom_init ? z : ldg16(S.momentum, offB);
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) mom[i][j] = 0.f;
-
-  for (int tb = t0 + rg; tb < t1; tb += 16 * kRB) {
-    uint2 up[kRB], un[kRB], uo[kRB];
-#pragma unroll
-    for (int i = 0; i < kRB; ++i) {
-      const int t = min(tb + 16 * i, t1 - 1);  // clamped: rows past t1 load a valid row, never stored
-      const int64_t off = (int64_t)t * kOdeD + c0;
-      up[i] = n_pos <= 1 ? ldraw(S.v_pos[0], off) : make_uint2(0u, 0u);
-      if (cfg) {
-        un[i] = n_neg <= 1 ? ldraw(S.v_neg[0], off) : make_uint2(0u, 0u);
-        uo[i] = mom_init ? make_uint2(0u, 0u) : ldraw(S.momentum, off);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kRB; ++i) {
-      const int t = tb + 16 * i;
-      if (t >= t1) break;
-      const int64_t off = (int64_t)t * kOdeD + c0;
-      const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
-      float vp[4];
-      if (n_pos <= 1) unpack4(up[i], vp);
-      else blend(S.v_pos, S.w_pos, n_pos, off, t, vp);
-      st4(vp_s, loc, vp);
-      if (cfg) {
-        float vn[4], ro[4], r[4];
-        if (n_neg <= 1) unpack4(un[i], vn);
-        else blend(S.v_neg, S.w_neg, n_neg, off, t, vn);
-        if (cache_neg) st4(S.neg_cache, off, vn);
-        unpack4(uo[i], ro);
-        const float mt = rnd(curve(S.apg_mom, S.apg_mom_s, t));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = mom_init ? rnd(vp[j] - vn[j]) : rnd(rnd(vp[j] - vn[j]) + rnd(mt * ro[j]));
-        st4(S.momentum, off, r);
-        st4(r_s, loc, r);
-        const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
-        const float w2 = w * w;
+      for (int h = 0; h < 2; ++h) {
+        if (h == 1 && !hasB) break;
+        const int t = h ? tB : tA;
+        const int64_t off = h ? offB : offA;
+        uint32_t vp[4], vn[4], mo[4], r[4];
+        words(h ? vpB : vpA, vp);
+        words(h ? vnB : vnA, vn);
+        words(h ? moB : moA, mo);
+        if (cache_neg) stg16(S.neg_cache, off, h ? vnB : vnA);
+        // r = bf16(bf16(v_pos - v_neg) + bf16(m_t * r_old))  (MomentumBuffer.update, ode_steps.py:276-300)
+        const uint32_t mt2 = bf2_dup(rnd(curve(S.apg_mom, S.apg_mom_s, t)));
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float pp = vp[j] * vp[j], pr = vp[j] * r[j], rr = r[j] * r[j];
-          mom[0][j] += rr;
-          mom[1][j] += pp;
-          mom[2][j] += pr;
-          mom[3][j] = fmaf(w, pp, mom[3][j]);
-          mom[4][j] = fmaf(w2, pp, mom[4][j]);
-          mom[5][j] = fmaf(w, pr, mom[5][j]);
-          mom[6][j] = fmaf(w2, pr, mom[6][j]);
-          mom[7][j] = fmaf(w2, rr, mom[7][j]);
+          const uint32_t d = sub_bf2(vp[j], vn[j]);
+          r[j] = mom_init ? d : add_bf2(d, mul_bf2(mt2, mo[j]));
         }
+        // the new momentum goes to global memory in phase 2 (from r_s): no global store is
+        // pending when the cluster barriers (release semantics) run
+        sts16(r_s, (int64_t)(t - t0) * kOdeD + c0, make_uint4(r[0], r[1], r[2], r[3]));
       }
     }
   }
+  __syncthreads();
 
-  // ---------------- cluster reduction of the moments (CFG slots only) -------
+  // ---------------- moments (CFG slots): per channel over the CTA's rows -------------------
   if (cfg) {
-    const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float o = __shfl_xor_sync(0xffffffffu, mom[i][j], 16);
-        if (lane < 16) sh.warp_part[warp][lane][i * 4 + j] = mom[i][j] + o;
-      }
+    const int c = tid & 63, g = tid >> 6;
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f, m5 = 0.f, m6 = 0.f, m7 = 0.f;
+    const __nv_bfloat16* vpc = vp_s + c;
+    const __nv_bfloat16* rc = r_s + c;
+    for (int t = t0 + g; t < t1; t += 4) {
+      const int64_t loc = (int64_t)(t - t0) * kOdeD;
+      const float vp = __bfloat162float(vpc[loc]), r = __bfloat162float(rc[loc]);
+      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f, w2 = w * w;
+      const float pp = vp * vp, pr = vp * r, rr2 = r * r;
+      m0 += rr2;
+      m1 += pp;
+      m2 += pr;
+      m3 = fmaf(w, pp, m3);
+      m4 = fmaf(w2, pp, m4);
+      m5 = fmaf(w, pr, m5);
+      m6 = fmaf(w2, pr, m6);
+      m7 = fmaf(w2, rr2, m7);
+    }
+    float* gp = sh.gpart[g][c];
+    gp[0] = m0;
+    gp[1] = m1;
+    gp[2] = m2;
+    gp[3] = m3;
+    gp[4] = m4;
+    gp[5] = m5;
+    gp[6] = m6;
+    gp[7] = m7;
     __syncthreads();
-    for (int e = tid; e < 16 * 32; e += kOdeThreads) {
-      const int g = e >> 5, q = e & 31;  // channel group, (moment, channel-in-group)
-      double sacc = 0.0;
-      for (int w = 0; w < kOdeThreads / 32; ++w) sacc += (double)sh.warp_part[w][g][q];
-      sh.cta_part[g * 4 + (q & 3)][q >> 2] = sacc;
+    for (int e = tid; e < kOdeD * 8; e += kOdeThreads) {
+      const int cc = e >> 3, i = e & 7;
+      double acc = 0.0;
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) acc += (double)sh.gpart[gg][cc][i];
+      sh.cta_part[cc][i] = acc;
     }
   }
   cluster.sync();  // partial moments of every CTA are visible cluster-wide
@@ -312,7 +325,7 @@ __global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOde
   }
   cluster.sync();  // peers finished reading our partials; constants visible in the CTA
 
-  // ---------------- phase 2: guidance, integration, next decoder input -----
+  // ---------------- phase 2: guidance, integration, next decoder input ----------------------
   const float tc = S.t_curr, tn = S.t_next, dt = tn - tc;
   const bool x0path = (flags & DEMON_ODE_X0PATH) != 0, mask = (flags & DEMON_ODE_MASK) != 0;
   const bool final_step = (flags & DEMON_ODE_FINAL) != 0;
@@ -325,131 +338,144 @@ __global__ void __launch_bounds__(kOdeThreads, 2) ode_step_kernel(const DemonOde
   const bool need_noise = !final_step && (sde_curve || (sde_bare && !mask) || (onc_on && !sde_bare));
   const bool noise_in = need_noise && S.noise != nullptr;
   const bool need_mask_data = mask || dec_mask;
-  float kc[4], ac[4], sc[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    kc[j] = cfg ? sh.k[c0 + j] : 0.f;
-    ac[j] = cfg ? sh.a[c0 + j] : 0.f;
-    sc[j] = cfg ? sh.sigma[c0 + j] : 0.f;
-  }
 
-  for (int tb = t0 + rg; tb < t1; tb += 16 * kRB) {
-    uint2 ux[kRB], uor[kRB], unz[kRB], usrc[kRB], utg[kRB], ueps[kRB], ug[kRB];
+  for (int t = t0 + rr; t < t1; t += 32) {
+    const int64_t off = (int64_t)t * kOdeD + c0;
+    const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    // every global load of the row first
+    const uint4 ux = ldg16(S.xt, off);
+    const uint4 uo = need_mask_data ? ldg16(S.mask_orig, off) : z;
+    const uint4 unz = need_mask_data ? ldg16(S.mask_noise, off) : z;
+    const uint4 usrc = sde_curve ? ldg16(S.source, off) : z;
+    const uint4 utg = (x0path && x0t) ? ldg16(S.x0_target, off) : z;
+    const uint4 ueps = noise_in ? ldg16(S.noise, off) : z;
+    const uint4 ug = (dec_out && gain) ? ldg16(gain, off) : z;
+    uint32_t vt[4], x[4], o[4], nz[4];
+    words(lds16(vp_s, loc), vt);
+    words(ux, x);
+    words(uo, o);
+    words(unz, nz);
+    if (cfg) {  // v_g = v + w (k r - a v), then cfg_rescale; rounded once (apg_forward + cfg_rescale)
+      uint32_t r[4];
+      const uint4 rv = lds16(r_s, loc);
+      stg16(S.momentum, off, rv);
+      words(rv, r);
+      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
+      const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
 #pragma unroll
-    for (int i = 0; i < kRB; ++i) {
-      const int t = min(tb + 16 * i, t1 - 1);
-      const int64_t off = (int64_t)t * kOdeD + c0;
-      ux[i] = ldraw(S.xt, off);
-      if (need_mask_data) {
-        uor[i] = ldraw(S.mask_orig, off);
-        unz[i] = ldraw(S.mask_noise, off);
+      for (int j = 0; j < 4; ++j) {
+        const int c = c0 + 2 * j;
+        const float2 kk = make_float2(sh.k[c], sh.k[c + 1]), aa = make_float2(sh.a[c], sh.a[c + 1]);
+        const float2 v2 = bf2_f2(vt[j]), r2 = bf2_f2(r[j]);
+        const float2 inner = fma_f2(make_float2(-aa.x, -aa.y), v2, mul_f2(kk, r2));
+        float2 vg = fma_f2(f2_dup(w), inner, v2);
+        if (resc) {
+          const float2 ss = make_float2(sh.sigma[c], sh.sigma[c + 1]);
+          vg = fma_f2(f2_dup(rho), mul_f2(vg, ss), mul_f2(f2_dup(1.0f - rho), vg));
+        }
+        vt[j] = f2_bf2(vg);
       }
-      if (sde_curve) usrc[i] = ldraw(S.source, off);
-      if (x0path && x0t) utg[i] = ldraw(S.x0_target, off);
-      if (noise_in) ueps[i] = ldraw(S.noise, off);
-      if (dec_out && gain) ug[i] = ldraw(gain, off);
     }
+    const float m = mask ? rnd(__ldg(S.mask + t) * S.mask_s) : 1.f;
+    const uint32_t m2 = bf2_dup(m), om2 = bf2_dup(rnd(1.0f - m));
+    if (mask) {  // mask_pre_blend at t_curr
 #pragma unroll
-    for (int i = 0; i < kRB; ++i) {
-      const int t = tb + 16 * i;
-      if (t >= t1) break;
-      const int64_t off = (int64_t)t * kOdeD + c0;
-      const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
-      float vt[4], x[4], o[4], nz[4];
-      ld4(vp_s, loc, vt);
-      if (cfg) {
-        float r[4];
-        ld4(r_s, loc, r);
-        const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
-        const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
+      for (int j = 0; j < 4; ++j) x[j] = pre_blend2(x[j], nz[j], o[j], m2, om2, tc);
+    }
+    const float vs = vs_on ? rnd(curve(S.vscale, S.vscale_s, t)) : 1.f;
+    const float onc = onc_on ? rnd(curve(S.onc, S.onc_s, t)) : 0.f;
+    float2 eps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    if (need_noise) {
+      if (noise_in) {
+        uint32_t ew[4];
+        words(ueps, ew);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) eps[j] = bf2_f2(ew[j]);
+      } else {
+        float z0[4], z1[4];
+        philox_normal4(S.seed, S.step, (uint64_t)off >> 2, z0);
+        philox_normal4(S.seed, S.step, ((uint64_t)off >> 2) + 1, z1);
+        eps[0] = make_float2(z0[0], z0[1]);
+        eps[1] = make_float2(z0[2], z0[3]);
+        eps[2] = make_float2(z1[0], z1[1]);
+        eps[3] = make_float2(z1[2], z1[3]);
+      }
+    }
+    uint32_t xn[4];
+    if (!x0path) {  // step_ode_euler (ode_steps.py:191-216): x + dt (v vs) + eps onc t_next
+      const float en = onc * tn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 v = mul_f2(bf2_f2(vt[j]), f2_dup(vs));
+        const float2 a1 = fma_f2(f2_dup(dt), v, bf2_f2(x[j]));
+        xn[j] = f2_bf2(fma_f2(eps[j], f2_dup(en), a1));
+      }
+    } else {
+      uint32_t x0[4];
+      const uint32_t vs2 = bf2_dup(vs);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)  // x0_from_vel: bf16(x - bf16(bf16(v vs) t_curr))
+        x0[j] = sub_bf2(x[j], scal_bf2(tc, mul_bf2(vt[j], vs2)));
+      if (mask) {  // mask_post_blend_x0: bf16(bf16(m x0) + bf16((1 - m) orig))
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x0[j] = add_bf2(mul_bf2(m2, x0[j]), mul_bf2(om2, o[j]));
+      }
+      if (x0t) {  // blend_x0_target / scalar x0 strength: bf16(bf16((1 - c) x0) + bf16(c target))
+        uint32_t tg[4];
+        words(utg, tg);
+        const float c = rnd(curve(S.x0_coef, S.x0_coef_s, t) * S.x0_coef_mul);
+        const uint32_t c2 = bf2_dup(c), oc2 = bf2_dup(rnd(1.0f - c));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x0[j] = add_bf2(mul_bf2(oc2, x0[j]), mul_bf2(c2, tg[j]));
+      }
+      if (sde_curve) {  // step_sde_curve: sdc (t eps + (1-t) x0) + (1 - sdc)(t eps + (1-t) src)
+        uint32_t src[4];
+        words(usrc, src);
+        const float sdc = rnd(curve(S.sdc, S.sdc_s, t));
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float vg = vt[j] + w * (kc[j] * r[j] - ac[j] * vt[j]);
-          if (resc) vg = rho * (vg * sc[j]) + (1.0f - rho) * vg;
-          vt[j] = rnd(vg);
+          const float2 te = mul_f2(f2_dup(tn), eps[j]);
+          const float2 full = fma_f2(f2_dup(1.0f - tn), bf2_f2(x0[j]), te);
+          const float2 srcn = fma_f2(f2_dup(1.0f - tn), bf2_f2(src[j]), te);
+          xn[j] = f2_bf2(fma_f2(f2_dup(sdc), full, mul_f2(f2_dup(1.0f - sdc), srcn)));
+        }
+      } else if (final_step) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xn[j] = x0[j];
+      } else if (sde_bare) {  // step_sde_renoise: t noise + (1 - t) x0
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 nn = mask ? bf2_f2(nz[j]) : eps[j];
+          xn[j] = f2_bf2(fma_f2(f2_dup(1.0f - tn), bf2_f2(x0[j]), mul_f2(f2_dup(tn), nn)));
+        }
+      } else {  // v_blended = bf16(bf16(x - x0) / t_curr), then the Euler step (stream.py:1269-1273)
+        const float en = onc * tn;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 d = bf2_f2(sub_bf2(x[j], x0[j]));
+          const float2 vb = bf2_f2(pack_bf16x2(__fdiv_rn(d.x, tc), __fdiv_rn(d.y, tc)));
+          const float2 a1 = fma_f2(f2_dup(dt), vb, bf2_f2(x[j]));
+          xn[j] = f2_bf2(fma_f2(eps[j], f2_dup(en), a1));
         }
       }
-      unpack4(ux[i], x);
-      if (need_mask_data) {
-        unpack4(uor[i], o);
-        unpack4(unz[i], nz);
+    }
+    stg16(S.xt, off, make_uint4(xn[0], xn[1], xn[2], xn[3]));
+    if (dec_out) {
+      uint32_t d[4] = {xn[0], xn[1], xn[2], xn[3]};
+      if (dec_mask) {  // mask_pre_blend at t_next with the next step's strength
+        const float mn = rnd(__ldg(S.mask + t) * S.mask_s_next);
+        const uint32_t mn2 = bf2_dup(mn), omn2 = bf2_dup(rnd(1.0f - mn));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[j] = pre_blend2(d[j], nz[j], o[j], mn2, omn2, tn);
       }
-      const float m = mask ? rnd(__ldg(S.mask + t) * S.mask_s) : 1.f;
-      if (mask) {  // mask_pre_blend at t_curr (ode_steps.py:89-106), op by op
-        const float om = rnd(1.0f - m), ot = 1.0f - tc;
+      if (gain) {
+        uint32_t g[4];
+        words(ug, g);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x[j] = rnd(rnd(m * x[j]) + rnd(om * rnd(rnd(tc * nz[j]) + rnd(ot * o[j]))));
+        for (int j = 0; j < 4; ++j) d[j] = mul_bf2(d[j], g[j]);
       }
-      const float vs = vs_on ? rnd(curve(S.vscale, S.vscale_s, t)) : 1.f;
-      const float onc = onc_on ? rnd(curve(S.onc, S.onc_s, t)) : 0.f;
-      float eps[4] = {0.f, 0.f, 0.f, 0.f};
-      if (need_noise) {
-        if (noise_in) unpack4(ueps[i], eps);
-        else philox_normal4(S.seed, S.step, (uint64_t)off >> 2, eps);
-      }
-      float xn[4];
-      if (!x0path) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) xn[j] = x[j] + dt * (vt[j] * vs) + eps[j] * onc * tn;
-      } else {
-        float x0[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x0[j] = rnd(x[j] - rnd(rnd(vt[j] * vs) * tc));
-        if (mask) {
-          const float om = rnd(1.0f - m);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) x0[j] = rnd(rnd(m * x0[j]) + rnd(om * o[j]));
-        }
-        if (x0t) {
-          float tg[4];
-          unpack4(utg[i], tg);
-          const float c = rnd(curve(S.x0_coef, S.x0_coef_s, t) * S.x0_coef_mul);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) x0[j] = lerp_eager(x0[j], c, tg[j]);
-        }
-        if (sde_curve) {
-          float src[4];
-          unpack4(usrc[i], src);
-          const float sdc = rnd(curve(S.sdc, S.sdc_s, t));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float full = tn * eps[j] + (1.0f - tn) * x0[j];
-            const float srcn = tn * eps[j] + (1.0f - tn) * src[j];
-            xn[j] = sdc * full + (1.0f - sdc) * srcn;
-          }
-        } else if (final_step) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) xn[j] = x0[j];
-        } else if (sde_bare) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) xn[j] = tn * (mask ? nz[j] : eps[j]) + (1.0f - tn) * x0[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float vb = rnd(__fdiv_rn(rnd(x[j] - x0[j]), tc));
-            xn[j] = x[j] + dt * vb + eps[j] * onc * tn;
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) xn[j] = rnd(xn[j]);
-      st4(S.xt, off, xn);
-      if (dec_out) {
-        float d[4] = {xn[0], xn[1], xn[2], xn[3]};
-        if (dec_mask) {  // mask_pre_blend at t_next with the next step's strength
-          const float mn = rnd(__ldg(S.mask + t) * S.mask_s_next);
-          const float om = rnd(1.0f - mn), ot = 1.0f - tn;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) d[j] = rnd(rnd(mn * d[j]) + rnd(om * rnd(rnd(tn * nz[j]) + rnd(ot * o[j]))));
-        }
-        if (gain) {
-          float gg[4];
-          unpack4(ug[i], gg);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) d[j] = d[j] * gg[j];
-        }
-        st4(S.dec_out, off, d);
-      }
+      stg16(S.dec_out, off, make_uint4(d[0], d[1], d[2], d[3]));
     }
   }
 }
@@ -462,7 +488,7 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   DEMON_CHECK_ARG(T > 0 && T <= kOdeMaxT, "ode: 0 < T <= %d required (T=%lld)", kOdeMaxT, (long long)T);
   DEMON_CHECK_ARG(n <= 65535 / kOdeCluster, "ode: too many slots (%d)", n);
   DEMON_CHECK_ARG(((uintptr_t)slots & 7) == 0, "ode: slot table must be 8-byte aligned");
-  DEMON_CHECK_ARG(!gain || ((uintptr_t)gain & 7) == 0, "ode: gain must be 8-byte aligned");
+  DEMON_CHECK_ARG(!gain || ((uintptr_t)gain & 15) == 0, "ode: gain must be 16-byte aligned");
   const int Tc = (int)((T + kOdeCluster - 1) / kOdeCluster);
   const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16);
   static std::atomic<uint64_t> attr_done{0};

@@ -200,6 +200,14 @@ class OdeTick:
             raise ValueError("too many slots for this OdeTick")
         if s.xt.shape != (self.T, self.D) or s.xt.dtype != torch.bfloat16 or not s.xt.is_contiguous():
             raise ValueError(f"xt must be a contiguous bf16 [{self.T}, {self.D}] tensor")
+        # the kernel moves latents in 16-byte vectors: every latent must start 16-byte aligned
+        lat = [s.xt, s.neg_cached, s.initial_noise, s.momentum, s.neg_cache_out, s.source, s.x0_target, s.noise,
+               s.dec_out] + [v for v, _ in s.pos] + [v for v, _ in (s.neg or [])]
+        if s.mask is not None:
+            lat += [s.mask.original, s.mask.noise]
+        for t in lat:
+            if t is not None and (t.data_ptr() % 16 or not t.is_contiguous()):
+                raise ValueError("slot latents must be contiguous and 16-byte aligned")
         self.slots.append(s)
 
     # ------------------------------------------------------------------
