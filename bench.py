@@ -612,7 +612,7 @@ def gemm_roofline(dit, dev, B):
         e0.record()
         out = orig(a, w, *args, **kw)
         e1.record()
-        rec.append((2.0 * a.rows * w.rows * a.K, e0, e1))
+        rec.append((2.0 * a.rows * w.rows * a.K, e0, e1, (a.rows, w.rows, a.K)))
         return out
     g = torch.Generator(device=dev).manual_seed(3)
     x = torch.randn(B, T5, 64, generator=g, device=dev).to(torch.bfloat16)
@@ -629,7 +629,21 @@ def gemm_roofline(dit, dev, B):
     torch.cuda.synchronize()
     flops = sum(r[0] for r in rec)
     ms = sum(r[1].elapsed_time(r[2]) for r in rec)
-    return {"launches": len(rec), "flops": flops, "ms": ms, "achieved": flops / (ms * 1e-3) / 1e12}
+    # DRAM traffic of the forward's GEMMs: ncu's per-launch bytes at M=12000 for each (N, K),
+    # scaled by the launch's rows; launches of other shapes are counted in traffic_flops_covered
+    traffic, covered = None, 0.0
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        per = json.loads(tf.read_text()).get("gemm_M12000", {})
+        traffic = 0.0
+        for fl, _, _, (m, n, k) in rec:
+            b = per.get(f"{n}x{k}")
+            if b is not None:
+                traffic += b * m / 12000.0
+                covered += fl
+    alg = sum(m * k * 0.5625 + n * k * 0.5625 + m * n * 2 for _, _, _, (m, n, k) in rec)
+    return {"launches": len(rec), "flops": flops, "ms": ms, "achieved": flops / (ms * 1e-3) / 1e12,
+            "alg_bytes": alg, "traffic": traffic, "traffic_flops_covered": covered / flops if flops else 0.0}
 
 
 def count_launches(fn):
@@ -811,7 +825,13 @@ def run_stream(args):
             "config": dict(CONFIG5, parallelism=f"slot-sharded ring x{world} ({RING // world} slots per GPU)",
                            prefill_ticks=STEPS5),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                         "frac": achieved / fp4_peak, "traffic": None,
+                         "frac": achieved / fp4_peak, "traffic": groof["traffic"],
+                         "traffic_note": "DRAM bytes of all GEMM launches of one forward: ncu "
+                                         "dram__bytes_read+write per launch at M=12000 for each (N, K), scaled "
+                                         "by the launch's rows (profiles/traffic.json); covers "
+                                         f"{100 * groof['traffic_flops_covered']:.1f} % of the GEMM FLOPs; "
+                                         "algorithmic bytes (operands + bf16 outputs) "
+                                         f"{groof['alg_bytes'] / 1e9:.2f} GB",
                          "peak_note": "FP4 dense peak taken as 4x the measured sustained bf16 cuBLAS figure "
                                       f"({pk.get('bf16_sustained', pk['bf16_tflops']):.0f} TF/s, of measured: the "
                                       f"GEMMs run inside a long step); nominal 9 PF/s -> frac {achieved / 9000.0:.3f}",
@@ -857,23 +877,86 @@ def run_reference_stream(args):
     }), flush=True)
 
 
+def run_kernel_workload(args):
+    """Kernel-level workloads (one GPU), also the commands the ncu summaries under profiles/ use:
+    ``gemm``: NVFP4 linears of shapes ``--shape M,N,K[:M,N,K...]`` (inputs quantised and weights
+    packed before timing), launched shape by shape in each warm-up and timed pass;
+    ``rows``: the 64-slot ODE step, the AdaLN-RMSNorm quantiser on [12000, 2048], SiLU*up on
+    [12000, 12288] and the activation quantiser on [12000, 2048].  Prints per-launch times."""
+    import torch
+    from demon_b200 import _build, _native as nat, nvfp4
+    _build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    launches = []
+    if args.workload == "gemm":
+        for shape in args.shape.split(":"):
+            M, N, K = (int(v) for v in shape.split(","))
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            a, pw = nvfp4.quantize(x), nvfp4.pack_weight(w)
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            launches.append((f"gemm {M}x{N}x{K}", 2.0 * M * N * K,
+                             lambda a=a, pw=pw, out=out: nvfp4.gemm(a, pw, out=out)))
+    else:
+        from demon_b200.rowops import adanorm_quantize, silu_mul_quantize
+        tick, nbytes, gain = ode_workload(dev, nslots=64, T=1500, seed=0)
+        b, nb = tick._stage()
+        tick._dev[b][:nb].copy_(tick._host[b][:nb])
+        M, D, F = 12000, 2048, 6144
+        h = torch.randn(M, D, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        sc = torch.ones(16, D, device=dev, dtype=torch.bfloat16)
+        sh = torch.zeros(16, D, device=dev, dtype=torch.bfloat16)
+        gu = torch.randn(M, 2 * F, generator=g, device=dev).to(torch.bfloat16)
+        launches += [
+            ("ode_step", nbytes, lambda: nat.check(nat.load().demon_ode_step(
+                tick._dev[b].data_ptr(), len(tick.slots), tick.T, 64, nat.ptr(gain), nat.stream_ptr()))),
+            ("adanorm_quantize", M * D * 2.5625 + M * 4, lambda: adanorm_quantize(h, w, 1e-6, sc, sh, 750)),
+            ("silu_mul_quantize", M * 2 * F * 2 + M * F * 0.5625 + M * 4, lambda: silu_mul_quantize(gu, F)),
+            ("quantize", M * D * 2.5625 + M * 4, lambda: nvfp4.quantize(h)),
+        ]
+    for _ in range(max(args.warmup, 3)):
+        for _, _, f in launches:
+            f()
+    torch.cuda.synchronize()
+    res = {}
+    for name, work, f in launches:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        unit = "TFLOP/s" if args.workload == "gemm" else "GB/s"
+        res[name] = {"us": us, unit: work / (us * 1e-6) / (1e12 if args.workload == "gemm" else 1e9)}
+    print(json.dumps({"workload": args.workload, "shape": args.shape, "steps": args.steps, "kernels": res,
+                      "device_status": list(nat.device_status())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stream", choices=["stream", "linear"])
+    ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows"])
+    ap.add_argument("--shape", default="12000,6144,2048", help="M,N,K[:M,N,K...] of --workload gemm")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-ode", dest="ode", action="store_false", help="skip the ODE-step roofline leg")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.workload == "stream" else 2000
+        args.steps = {"stream": 20, "linear": 2000}.get(args.workload, 10)
     if args.warmup is None:
         args.warmup = 3 if args.workload == "stream" else 10
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         (run_reference_stream if args.workload == "stream" else run_reference)(args)
+        return
+    if args.workload in ("gemm", "rows"):
+        run_kernel_workload(args)
         return
     (run_stream if args.workload == "stream" else run_linear)(args)
 
