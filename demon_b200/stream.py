@@ -167,7 +167,8 @@ class GraphedDecoder:
 @dataclass
 class StreamConfig:
     """The DiffusionConfig fields the tick reads (acestep/engine/diffusion.py:13-59).
-    DCW (on by default in the reference) is not part of this path: see DESIGN.md."""
+    DCW (on by default in the reference, dcw.py:428-490) is not applied: the tick here is the
+    reference's tick with ``dcw_enabled=False``."""
     infer_steps: int = 8
     infer_method: str = "ode"
     shift: float = 3.0
