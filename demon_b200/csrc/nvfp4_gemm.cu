@@ -67,6 +67,7 @@ struct GemmParams {
   const __nv_bfloat16* rope_sin;
   float hn_eps;
   int m_tiles, n_tiles;
+  int m_group;  // tile order: bands of m_group m-blocks, each swept over every n-block
 };
 
 constexpr int kBM = 128;
@@ -105,6 +106,18 @@ struct GemmCfg {
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
 };
+
+// Tile t -> (m_blk, n_blk).  Tiles run in bands of m_group m-blocks: inside a band the
+// m-block varies fastest, then the n-block, so the CTAs working at one time share a band
+// of A rows (which stays in L2 while the band sweeps N) and a few B column blocks.  With
+// m_group = m_tiles this is plain m-fastest order.
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m_blk, int& n_blk) {
+  const int band = p.m_group * p.n_tiles;
+  const int b = t / band, j = t - b * band;
+  const int gm = min(p.m_group, p.m_tiles - b * p.m_group);
+  m_blk = b * p.m_group + j % gm;
+  n_blk = j / gm;
+}
 
 __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
   // K-major, 128-byte swizzle: 8-row core groups 1024 bytes apart.
@@ -195,7 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t kchunks = p.K / 64;
       bool ok = true;
       for (int tile = cid; ok && tile < num_tiles; tile += ncl) {
-        const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+        int m_blk, n_blk;
+        tile_coords(tile, p, m_blk, n_blk);
         const int m0 = m_blk * kTileM, n0 = n_blk * BN;
         const int am0 = m0 + (int)rank * kBM;                  // this CTA's A rows
         const int bn0 = n0 + (int)rank * (BN / 2) * (PAIR ? 1 : 0);  // this CTA's B rows
@@ -370,7 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     uint32_t it = 0, nstore = 0;
     for (int tile = cid; tile < num_tiles; tile += ncl, ++it) {
-      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      int m_blk, n_blk;
+      tile_coords(tile, p, m_blk, n_blk);
       const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;  // this CTA's 128 rows
       const int ncol0 = n0 + half * C::kColsPerWarp;
       // Everything that does not depend on the accumulator is fetched while the MMAs run:
@@ -577,6 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+constexpr int kBandMBlocks = 8;
+
 template <int BN, int STAGES, bool FP4, bool PAIR = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
                 const CUtensorMap& o, GemmParams p, cudaStream_t st, const CUtensorMap* sfa = nullptr,
@@ -595,6 +612,10 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   p.m_tiles = (p.M + tile_m - 1) / tile_m;
   p.n_tiles = (p.N + BN - 1) / BN;
   const int tiles = p.m_tiles * p.n_tiles;
+  // A operand bytes beyond ~24 MB do not survive in L2 next to the streaming output, so
+  // large-M launches sweep N in bands of 8 m-blocks; smaller ones keep m-fastest order
+  const double a_bytes = (double)p.M * p.K * (FP4 ? 0.5625 : 2.0);
+  p.m_group = (a_bytes > 24e6) ? std::min(p.m_tiles, kBandMBlocks) : p.m_tiles;
   CUtensorMap z;
   memset(&z, 0, sizeof z);
   if (!PAIR) {
