@@ -55,7 +55,7 @@ class DemonGemmArgs(ctypes.Structure):
         ("gate", _vp), ("gate_rows", _i64), ("ld_gate", _i64),
         ("lora_xa", _vp), ("lora_b", _vp), ("lora_rank", _i64),
         ("hn_cols", _i64), ("hn_q_cols", _i64), ("rope_S", _i64), ("hn_wq", _vp), ("hn_wk", _vp),
-        ("rope_cos", _vp), ("rope_sin", _vp), ("hn_eps", _f32), ("_pad1", _i32),
+        ("rope_cos", _vp), ("rope_sin", _vp), ("hn_eps", _f32), ("silu_mul", _i32),
     ]
 
 
@@ -121,7 +121,7 @@ def load() -> ctypes.CDLL:
         L.demon_bf16_linear.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp]
         L.demon_adanorm_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp,
                                              _vp, _i64, _vp]
-        L.demon_silu_mul_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]
+        L.demon_silu_mul_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp]
         L.demon_head_norm_rope.argtypes = [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _f32, _vp]
         for name in EXPORTED:
             getattr(L, name).restype = (_i64 if name in ("demon_nvfp4_sf_bytes", "demon_nvfp4_noalloc_scratch_bytes")

@@ -411,4 +411,19 @@ __device__ __forceinline__ uint32_t add_bf2(uint32_t a, uint32_t b) {
   return r;
 }
 
+// silu(g) = g / (1 + exp(-g)) in fp32 with the fast exponential and division intrinsics
+// (relative error a few fp32 ulps at every g, far below the bf16 rounding that follows; a
+// tanh form g/2 (1 + tanh(g/2)) would lose all relative accuracy for strongly negative g).
+// exp(-g) overflows to +inf for g < -88 and the quotient is then -0, the limit.
+__device__ __forceinline__ float silu_f32(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+// h = bf16(bf16(silu(g)) * u) for a pair of bf16 values (Qwen3MLP's act_fn(gate) * up):
+// silu rounded to bf16, then multiplied by up in bf16 (exact product, one rounding).  The
+// SwiGLU row kernel and the gate/up GEMM epilogue both use this, so the two paths give the
+// same bits.
+__device__ __forceinline__ uint32_t silu_mul_bf2(uint32_t g, uint32_t u) {
+  const float2 gf = bf2_f2(g);
+  return mul_bf2(pack_bf16x2(silu_f32(gf.x), silu_f32(gf.y)), u);
+}
+
 }  // namespace demon

@@ -151,29 +151,13 @@ struct SiluArgs {
   float* gs;
   uint8_t* codes;           // [M, F/2]
   uint8_t* sf;
+  __nv_bfloat16* y;         // optional bf16 h [M, ldy]
+  int64_t ldy;
 };
 
-__device__ __forceinline__ float tanh_approx(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ uint4 silu_mul8(uint4 g, uint4 u) {
-  const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // silu(g) = g * sigmoid(g) = g * (1/2 + tanh(g/2) / 2), one hardware tanh per element; the
-    // result is rounded to bf16 (8 significant bits), coarser than the approximation's error,
-    // then multiplied by up in bf16 (exact product, one rounding)
-    const float2 gf = bf2_f2(gw[i]);
-    const float2 hf = make_float2(0.5f * gf.x, 0.5f * gf.y);
-    const float2 th = make_float2(tanh_approx(hf.x), tanh_approx(hf.y));
-    const float2 sf = fma_f2(hf, th, hf);  // g/2 + g/2 * tanh(g/2)
-    o[i] = mul_bf2(f2_bf2(sf), uw[i]);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  return make_uint4(silu_mul_bf2(g.x, u.x), silu_mul_bf2(g.y, u.y), silu_mul_bf2(g.z, u.z),
+                    silu_mul_bf2(g.w, u.w));
 }
 
 // h = bf16(bf16(silu(gate)) * up) (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), turbo.py:34-35),
@@ -206,6 +190,15 @@ __global__ void __launch_bounds__(256) silu_mul_quant_kernel(const SiluArgs a) {
   for (int j = 0; j < 2 * G::NB; ++j) {
     gv[j] = silu_mul8(gv[j], uv[j]);
     am = fmaxf(am, absmax8_fast(gv[j]));
+  }
+  if (a.y && live) {
+    uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
+#pragma unroll
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t c = 2 * ((int64_t)(wr * G::NB + j) * 32 + lane);
+      yrow[c] = gv[2 * j];
+      yrow[c + 1] = gv[2 * j + 1];
+    }
   }
   am = row_reduce<G::W, true>(am, red, warp, lane);
   if (m >= a.Mpad) return;
@@ -367,12 +360,14 @@ extern "C" int demon_adanorm_quantize(const void* x, int64_t M, int64_t D, int64
 }
 
 extern "C" int demon_silu_mul_quantize(const void* gu, int64_t M, int64_t F, int64_t ld, float* gs, uint8_t* codes,
-                                       uint8_t* sf, void* stream) {
+                                       uint8_t* sf, void* y, int64_t ldy, void* stream) {
   DEMON_API_BEGIN();
   DEMON_CHECK_ARG(M >= 0 && row_width_ok(F), "silu_mul: F must be one of 256 ... 8192 (F=%lld)", (long long)F);
   DEMON_CHECK_ARG(gu && gs && codes && sf, "silu_mul: null pointer");
   DEMON_CHECK_ARG(ld >= 2 * F && ld % 8 == 0 && ((uintptr_t)gu & 15) == 0,
                   "silu_mul: ld >= 2F, ld %% 8 == 0, 16-byte aligned input");
+  DEMON_CHECK_ARG(!y || (ldy >= F && ldy % 8 == 0 && ((uintptr_t)y & 15) == 0),
+                  "silu_mul: y needs ldy >= F, ldy %% 8 == 0, 16-byte alignment");
   SiluArgs a{};
   a.gu = reinterpret_cast<const __nv_bfloat16*>(gu);
   a.M = M;
@@ -381,6 +376,8 @@ extern "C" int demon_silu_mul_quantize(const void* gu, int64_t M, int64_t F, int
   a.gs = gs;
   a.codes = codes;
   a.sf = sf;
+  a.y = reinterpret_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
   if (a.Mpad == 0) return DEMON_OK;
   DEMON_CHECK_ARG(launch_silu(F, a, reinterpret_cast<cudaStream_t>(stream)) == DEMON_OK,
                   "silu_mul: unsupported width %lld", (long long)F);

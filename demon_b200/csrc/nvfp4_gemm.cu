@@ -68,6 +68,7 @@ struct GemmParams {
   float hn_eps;
   int m_tiles, n_tiles;
   int m_group;  // tile order: bands of m_group m-blocks, each swept over every n-block
+  int silu_mul;  // SwiGLU epilogue: interleaved gate/up blocks of 128 -> h of width N / 2
 };
 
 constexpr int kBM = 128;
@@ -131,6 +132,8 @@ __device__ __forceinline__ uint64_t sf_desc(const void* p) {
 // the TMA 64-byte swizzle (address bits [4,5] ^= bits [7,8]).
 __device__ __forceinline__ int stg_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
+// One CTA per SM (persistent).  10 warps spread over the SM's 4 sub-partitions put 3 warps on
+// two of them, so a thread gets at most 168 of a sub-partition's 16 K registers.
 template <int BN, int STAGES, bool FP4, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -383,6 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t hnv = smem_u32(smem + C::offHn) + ew * (C::kColsPerWarp * 4);
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     uint32_t it = 0, nstore = 0;
+    // SwiGLU: a BN = 256 tile holds gate block n and up block n of the interleaved weight; each
+    // warp takes 64 output columns (its 64 gate and the matching 64 up accumulator columns)
+    const bool sm = FP4 && BN == 256 && p.silu_mul != 0;
     for (int tile = cid; tile < num_tiles; tile += ncl, ++it) {
       int m_blk, n_blk;
       tile_coords(tile, p, m_blk, n_blk);
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
       // the lane's row scale, and L2 prefetches of its gate / residual row segments.
       for (int i = lane; i < C::kColsPerWarp; i += 32) {
-        const int n = ncol0 + i;
+        const int n = sm ? n0 + (i < 64 ? half * 64 + i : 128 + half * 64 + (i - 64)) : ncol0 + i;
         float cv = 0.0f;
         if (n < p.N)
           cv = (FP4 || !p.col_scale) ? (p.bias ? __bfloat162float(p.bias[n]) : 0.0f) : p.col_scale[n];
@@ -407,9 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int64_t row = (int64_t)m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const float alpha = (row_ok && p.a_gs)
-                              ? p.a_gs[p.a_gs_per_row ? row : 0] * p.w_gs[p.w_gs_per_block ? ncol0 >> 7 : 0]
-                              : 0.0f;
+      const int wblk = sm ? (n0 >> 7) : (ncol0 >> 7);  // weight-scale block of the (gate) columns
+      const float a_row = (row_ok && p.a_gs) ? p.a_gs[p.a_gs_per_row ? row : 0] : 0.0f;
+      const float alpha = (row_ok && p.a_gs) ? a_row * p.w_gs[p.w_gs_per_block ? wblk : 0] : 0.0f;
+      const float alpha_u = sm ? a_row * p.w_gs[p.w_gs_per_block ? wblk + 1 : 0] : alpha;
       const __nv_bfloat16* gate_row =
           (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
       const __nv_bfloat16* res_row = (FP4 && p.residual && row_ok) ? p.residual + row * p.ldr + ncol0 : nullptr;
@@ -425,7 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t v[C::kChunks][32];
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c)
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * C::kColsPerWarp + c * 32), v[c]);
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) +
+                               (uint32_t)(sm ? (c < 2 ? 0 : 128) + half * 64 + (c & 1) * 32
+                                             : half * C::kColsPerWarp + c * 32),
+                           v[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -447,7 +457,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 8; ++j) {
           const float4 cv = ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j));
           if (FP4) {
-            const float2 al = make_float2(alpha, alpha);
+            const float ac = (sm && c >= 2) ? alpha_u : alpha;
+            const float2 al = make_float2(ac, ac);
             y[c][2 * j] = f2_bf2(fma_f2(al, make_float2(__uint_as_float(v[c][4 * j]), __uint_as_float(v[c][4 * j + 1])),
                                         make_float2(cv.x, cv.y)));
             y[c][2 * j + 1] = f2_bf2(fma_f2(
@@ -466,6 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
+      if constexpr (FP4 && BN == 256) {
+        if (sm) {  // h = bf16(bf16(silu(g)) * u): chunks 0-1 gate, 2-3 the matching up columns
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int k = 0; k < 16; ++k) y[c][k] = silu_mul_bf2(y[c][k], y[c + 2][k]);
+        }
+      }
       if (hn) {
         // q_norm / k_norm: Qwen3RMSNorm over the row's 128 values of this head
         float2 s2 = make_float2(0.0f, 0.0f);
@@ -512,7 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
-        const int ncol = ncol0 + c * 32;
+        if (sm && c >= 2) break;  // SwiGLU: two 32-column output chunks per warp
+        const int ncol = sm ? (n0 >> 1) + half * 64 + c * 32 : ncol0 + c * 32;
         // FP4 tiles never cross N (N % BN == 0); the bf16 GEMM's last tile can (rank < BN)
         if (!FP4 && ncol >= p.N) break;
         if (FP4) {
@@ -674,8 +694,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   DEMON_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: dimension too large");
   DEMON_CHECK_ARG(a->a_codes && a->a_sf && a->a_gs && a->w_codes && a->w_sf && a->w_gs && a->out,
                   "gemm: null operand");
-  DEMON_CHECK_ARG(a->ldo >= N && a->ldo % 8 == 0 && ((uintptr_t)a->out & 15) == 0,
-                  "gemm: out needs ldo >= N, ldo %% 8 == 0, 16-byte alignment");
+  DEMON_CHECK_ARG(a->ldo >= (a->silu_mul ? N / 2 : N) && a->ldo % 8 == 0 && ((uintptr_t)a->out & 15) == 0,
+                  "gemm: out needs ldo >= N (N / 2 with silu_mul), ldo %% 8 == 0, 16-byte alignment");
   DEMON_CHECK_ARG(!a->residual || (a->ldr >= N && a->ldr % 8 == 0 && ((uintptr_t)a->residual & 15) == 0),
                   "gemm: residual needs ldr >= N, ldr %% 8 == 0, 16-byte alignment");
   DEMON_CHECK_ARG(!a->bias || ((uintptr_t)a->bias & 15) == 0, "gemm: bias must be 16-byte aligned");
@@ -700,6 +720,11 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                                      ((uintptr_t)a->rope_sin & 15) == 0),
                     "gemm: rotary tables need rope_sin, rope_S > 0 and 16-byte alignment");
   }
+  const bool silu = a->silu_mul != 0;
+  DEMON_CHECK_ARG(!silu || (N % 256 == 0 && !lora && a->hn_cols == 0 && !a->gate && !a->residual),
+                  "gemm: the SwiGLU epilogue needs N %% 256 == 0 and excludes LoRA, head norm, gate, residual");
+  const int64_t n_out = silu ? N / 2 : N;
+  DEMON_CHECK_ARG(!silu || a->ldo >= n_out, "gemm: SwiGLU output needs ldo >= N / 2");
   if (M == 0) return DEMON_OK;
 
   const bool bn256 = (N % 256 == 0);
@@ -725,7 +750,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   }
   // output: 32 x 32 bf16 store boxes (64-byte rows, 64-byte swizzle); rows past M are clipped
   CUtensorMap to;
-  DEMON_RC(make_tmap_2d(&to, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+  DEMON_RC(make_tmap_2d(&to, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)n_out, (uint64_t)M,
                         (uint64_t)a->ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   if (lora) {
     const uint64_t r = (uint64_t)a->lora_rank;
@@ -760,6 +785,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.rope_cos = reinterpret_cast<const __nv_bfloat16*>(a->rope_cos);
   p.rope_sin = reinterpret_cast<const __nv_bfloat16*>(a->rope_sin);
   p.hn_eps = a->hn_eps;
+  p.silu_mul = silu ? 1 : 0;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);

@@ -257,21 +257,25 @@ class MLP(nn.Module):
         self._fused = None
 
     def forward(self, a, xb, h, gate, S):
+        down_lora = self.down_proj.lora.active() is not None
         if not _has_lora(self.gate_proj, self.up_proj):
+            # one GEMM for gate and up (interleaved 128-row blocks) whose epilogue applies
+            # silu(g) * u; h is then quantised for down_proj like any activation
             if self._fused is None:
-                self._fused = Q.fuse_weights([_packed(self.gate_proj), _packed(self.up_proj)])
-            gu = Q.gemm(a, self._fused)
+                self._fused = Q.interleave_weights(_packed(self.gate_proj), _packed(self.up_proj))
+            hb = Q.gemm(a, self._fused, silu_mul=True)
+            ha = Q.quantize(hb)
         else:
-            outs = []
-            for l in (self.gate_proj, self.up_proj):
+            M = a.rows
+            gu = torch.empty((M, 2 * self.F), dtype=torch.bfloat16, device=h.device)
+            for i, l in enumerate((self.gate_proj, self.up_proj)):
                 xa, lb = _lora(l, xb, a)
-                outs.append(Q.gemm(a, _packed(l), lora_xa=xa, lora_b=lb))
-            gu = torch.cat(outs, 1)
-        ha = silu_mul_quantize(gu, self.F)
+                Q.gemm(a, _packed(l), lora_xa=xa, lora_b=lb, out=gu[:, i * self.F:(i + 1) * self.F])
+            hb = torch.empty((M, self.F), dtype=torch.bfloat16, device=h.device) if down_lora else None
+            ha = silu_mul_quantize(gu, self.F, y=hb)
         xa = lb = None
-        if self.down_proj.lora.active() is not None:
-            hb = torch.nn.functional.silu(gu[:, :self.F]) * gu[:, self.F:]
-            xa, lb = _lora(self.down_proj, hb.contiguous(), ha)
+        if down_lora:
+            xa, lb = _lora(self.down_proj, hb, ha)
         return Q.gemm(ha, _packed(self.down_proj), residual=h, gate=gate, gate_rows=S, lora_xa=xa, lora_b=lb)
 
 

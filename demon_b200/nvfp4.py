@@ -105,6 +105,23 @@ def fuse_weights(parts: list) -> NVFP4Tensor:
     return NVFP4Tensor(codes, sf, gs, sum(t.rows for t in parts), K, per_block=True)
 
 
+def interleave_weights(gate: NVFP4Tensor, up: NVFP4Tensor) -> NVFP4Tensor:
+    """Pack MLP gate and up projections for the GEMM's SwiGLU epilogue (``gemm(silu_mul=True)``):
+    rows in blocks of 128 alternate gate, up (gate 0..127, up 0..127, gate 128..255, ...), each
+    block keeping its part's global scale, so one 256-column tile holds the gate and up values
+    of the same 128 output features."""
+    K = gate.K
+    for t in (gate, up):
+        if t.K != K or t.rows != gate.rows or t.rows % 128 or t.per_row or t.per_block or t.gs.numel() != 1:
+            raise ValueError("interleave_weights: gate and up need equal shapes, rows % 128 == 0, one scale each")
+    nb = gate.rows // 128
+    codes = torch.stack([gate.codes.view(nb, 128, K // 2), up.codes.view(nb, 128, K // 2)], 1)
+    sf = torch.stack([gate.sf.view(nb, -1), up.sf.view(nb, -1)], 1)
+    gs = torch.stack([gate.gs.expand(nb), up.gs.expand(nb)], 1)
+    return NVFP4Tensor(codes.reshape(2 * gate.rows, K // 2).contiguous(), sf.reshape(-1).contiguous(),
+                       gs.reshape(-1).contiguous(), 2 * gate.rows, K, per_block=True)
+
+
 def bf16_linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """out = bf16(x @ w^T + bias) on the tensor cores, row by row independent of M.
@@ -143,8 +160,11 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, gate: torch.Tensor | None = None, gate_rows: int = 1,
          lora_xa: torch.Tensor | None = None, lora_b: torch.Tensor | None = None,
          out: torch.Tensor | None = None, head_norm: tuple | None = None, rope: tuple | None = None,
-         stream=None) -> torch.Tensor:
+         silu_mul: bool = False, stream=None) -> torch.Tensor:
     """out = residual + gate * (alpha * (A W^T + lora) + bias), bf16 [M, N].
+
+    ``silu_mul``: ``w`` from :func:`interleave_weights`; out = bf16(bf16(silu(g)) * u), bf16
+    [M, N/2], with g and u the gate / up projections (Qwen3MLP's act_fn(gate) * up).
 
     ``head_norm = (hn_cols, hn_q_cols, w_q, w_k, eps)``: per-head RMSNorm of the output's
     first hn_cols columns (heads of 128; w_q for the first hn_q_cols, w_k after), and with
@@ -155,8 +175,9 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
     M, N, K = a.rows, w.rows, a.K
     dev = a.codes.device
     if out is None:
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((M, N // 2 if silu_mul else N), dtype=torch.bfloat16, device=dev)
     args = nat.DemonGemmArgs()
+    args.silu_mul = int(bool(silu_mul))
     args.a_codes, args.a_sf, args.a_gs = nat.ptr(a.codes), nat.ptr(a.sf), nat.ptr(a.gs)
     args.a_gs_per_row = int(a.per_row)
     args.w_gs_per_block = int(w.per_block)

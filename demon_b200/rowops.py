@@ -45,13 +45,19 @@ def adanorm_quantize(x: torch.Tensor, norm_w: torch.Tensor, eps: float, scale1: 
     return q
 
 
-def silu_mul_quantize(gu: torch.Tensor, F: int, stream=None) -> NVFP4Tensor:
-    """NVFP4 of bf16(bf16(silu(gu[:, :F])) * gu[:, F:2F]) per row."""
+def silu_mul_quantize(gu: torch.Tensor, F: int, y: torch.Tensor | None = None, stream=None) -> NVFP4Tensor:
+    """NVFP4 of h = bf16(bf16(silu(gu[:, :F])) * gu[:, F:2F]) per row; ``y`` (bf16 [M, F],
+    unit column stride) also receives h."""
     _check_cuda_bf16(gu, "gu")
     M = gu.shape[0]
+    if y is not None:
+        _check_cuda_bf16(y, "y")
+        if y.shape[0] != M or y.shape[1] < F or y.stride(1) != 1:
+            raise ValueError("silu_mul_quantize: y must be [M, >= F] with unit column stride")
     q = _alloc_q(M, F, gu.device)
     nat.check(nat.load().demon_silu_mul_quantize(nat.ptr(gu), M, F, gu.stride(0), nat.ptr(q.gs), nat.ptr(q.codes),
-                                                 nat.ptr(q.sf), nat.stream_ptr(stream)))
+                                                 nat.ptr(q.sf), nat.ptr(y), y.stride(0) if y is not None else 0,
+                                                 nat.stream_ptr(stream)))
     return q
 
 

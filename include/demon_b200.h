@@ -132,7 +132,14 @@ typedef struct DemonGemmArgs {
   const void* rope_cos;
   const void* rope_sin;
   float hn_eps;
-  int32_t _pad1;
+  /* SwiGLU epilogue (silu_mul != 0): the weight's rows are gate and up blocks of 128
+   * interleaved (gate 0..127, up 0..127, gate 128..255, ...; nvfp4.interleave_weights), and
+   * the output is h = bf16(bf16(silu(g)) * u) of width N / 2 (out [M, ldo >= N / 2]) with
+   * g, u = bf16(alpha * acc + bias) of the paired columns -- Qwen3MLP's
+   * act_fn(gate_proj(x)) * up_proj(x) (turbo.py:34-35), bit-identical to
+   * demon_silu_mul_quantize's h.  Needs N % 256 == 0; excludes LoRA, head norm, gate,
+   * residual. */
+  int32_t silu_mul;
 } DemonGemmArgs;
 
 DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);
@@ -177,7 +184,7 @@ DEMON_API int demon_bf16_linear(const void* x, int64_t M, int64_t K, int64_t ldx
  *   D in {256, 512, 1024, 2048, 3072, 4096, 6144, 8192}.
  * demon_silu_mul_quantize: gu bf16 [M, ld] holds gate in columns [0, F) and up in [F, 2F);
  *   h = bf16(bf16(silu(gate)) * up), NVFP4-quantised per row (Qwen3MLP's act_fn(gate) * up,
- *   turbo.py:34-35).  F as D above.
+ *   turbo.py:34-35) and, when y is given, also stored as bf16 into y [M, ldy].  F as D above.
  * demon_head_norm_rope: in place on `heads` heads of 128 columns starting at col0 of
  *   x bf16 [M, ld]: Qwen3RMSNorm over each head (weight w [128]), then, when cos/sin
  *   (bf16 [S, 128], position = m % S) are given, x * cos + rotate_half(x) * sin with each
@@ -189,7 +196,7 @@ DEMON_API int demon_adanorm_quantize(const void* x, int64_t M, int64_t D, int64_
                                      float eps, float* gs, uint8_t* codes, uint8_t* sf, void* y, int64_t ldy,
                                      void* stream);
 DEMON_API int demon_silu_mul_quantize(const void* gu, int64_t M, int64_t F, int64_t ld, float* gs, uint8_t* codes,
-                                      uint8_t* sf, void* stream);
+                                      uint8_t* sf, void* y, int64_t ldy, void* stream);
 DEMON_API int demon_head_norm_rope(void* x, int64_t M, int64_t ld, int64_t col0, int64_t heads, const void* w,
                                    const void* cos, const void* sin, int64_t S, float eps, void* stream);
 

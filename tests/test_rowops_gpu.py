@@ -94,9 +94,11 @@ def test_silu_mul_quantize(cuda, M, F):
     from demon_b200.rowops import silu_mul_quantize
     g = torch.Generator().manual_seed(F)
     gu = (2 * torch.randn(M, 2 * F, generator=g)).to(torch.bfloat16)
-    q = silu_mul_quantize(gu.to(cuda), F)
+    y = torch.empty(M, F, dtype=torch.bfloat16, device=cuda)
+    q = silu_mul_quantize(gu.to(cuda), F, y=y)
     gf, uf = gu[:, :F].float(), gu[:, F:].float()
     h = bf(bf(gf / (1 + torch.exp(-gf))) * uf)
+    ulp_check(y, h)                    # silu in fp32 then two bf16 roundings, as torch's eager ops
     codes, sf_swz, sf_lin, gs = oracle_quant_of(h.to(torch.bfloat16))
     # codes follow h; h itself may differ by one ulp where exp rounds differently
     same = (q.codes.cpu().numpy() == codes).mean()
@@ -193,3 +195,36 @@ def test_gemm_head_norm_epilogue(cuda, rope):
     head_norm_rope(ref, hq * 128, hk, wk, 1e-6, **kw)
     ulp_check(fused[:, :(hq + hk) * 128], ref[:, :(hq + hk) * 128])
     assert torch.equal(fused[:, (hq + hk) * 128:], ref[:, (hq + hk) * 128:])
+
+
+@pytest.mark.parametrize("M,F,bias", [(300, 512, False), (7, 6144, False), (129, 1024, True)])
+def test_gemm_silu_epilogue(cuda, M, F, bias):
+    """The gate/up GEMM with the SwiGLU epilogue (interleaved weight blocks) gives exactly the
+    h of GEMM + demon_silu_mul_quantize, and quantising it gives the same NVFP4 operand."""
+    from demon_b200 import nvfp4 as Q
+    from demon_b200.rowops import silu_mul_quantize
+    K = 2048
+    g = torch.Generator().manual_seed(M + F)
+    x = make_x(M, K, 9).to(cuda)
+    wg = (torch.randn(F, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    wu = (torch.randn(F, K, generator=g) * 0.3).to(torch.bfloat16).to(cuda)
+    a, pg, pu = Q.quantize(x), Q.pack_weight(wg), Q.pack_weight(wu)
+    bg = bu = None
+    if bias:
+        bg = (0.5 * torch.randn(F, generator=g)).to(torch.bfloat16).to(cuda)
+        bu = (0.5 * torch.randn(F, generator=g)).to(torch.bfloat16).to(cuda)
+    b_cat = torch.cat([bg, bu]) if bias else None
+    b_il = torch.stack([bg.view(-1, 128), bu.view(-1, 128)], 1).reshape(-1) if bias else None
+    gu = Q.gemm(a, Q.fuse_weights([pg, pu]), bias=b_cat)
+    y = torch.empty(M, F, dtype=torch.bfloat16, device=cuda)
+    ref_q = silu_mul_quantize(gu, F, y=y)
+    h = Q.gemm(a, Q.interleave_weights(pg, pu), bias=b_il, silu_mul=True)
+    assert h.shape == (M, F)
+    assert torch.equal(h, y)
+    hq = Q.quantize(h)
+    assert torch.equal(hq.codes, ref_q.codes)
+    assert torch.equal(hq.sf, ref_q.sf)
+    assert torch.equal(hq.gs, ref_q.gs)
+    # and against the definition on the GEMM's own gate / up values
+    gf, uf = gu[:, :F].float().cpu(), gu[:, F:].float().cpu()
+    ulp_check(h, bf(bf(gf / (1 + torch.exp(-gf))) * uf))
