@@ -177,11 +177,11 @@ __device__ __forceinline__ void store_block(const QBlock& q, bool valid, int64_t
 
 // Geometry of the block-per-lane row kernels for a row of K elements: W warps per row, NB
 // blocks per lane; lane l of row-warp w owns blocks kb = (w * NB + j) * 32 + l (j < NB).
-// Rows shorter than 512 use the first K/16 lanes of one warp.
-template <int K>
+// Rows shorter than 512 use the first K/16 lanes of one warp.  WF != 0 fixes W.
+template <int K, int WF = 0>
 struct RowQ {
   static constexpr int kBPR = K / 16;
-  static constexpr int W = (kBPR % 128 == 0) ? 4 : (kBPR % 64 == 0) ? 2 : 1;
+  static constexpr int W = WF ? WF : (kBPR % 128 == 0) ? 4 : (kBPR % 64 == 0) ? 2 : 1;
   static constexpr int NB = kBPR >= 32 * W ? kBPR / (32 * W) : 1;
   static constexpr int R = 8 / W;  // rows per 256-thread CTA
   static_assert(kBPR % 4 == 0 && (kBPR < 32 || kBPR % (32 * W) == 0), "row width");
