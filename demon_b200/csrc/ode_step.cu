@@ -98,7 +98,10 @@ __device__ __forceinline__ void philox_normal4(uint64_t seed, uint64_t step, uin
 }
 
 struct OdeShared {
-  float gpart[4][kOdeD][8];     // per row-group moment partials (fp32 over the group's rows)
+  union {
+    float gpart[4][kOdeD][8];   // per row-group moment partials (fp32 over the group's rows)
+    double tot[kOdeD][8];       // then: the slot's moments, summed over the cluster
+  };
   double cta_part[kOdeD][8];    // this CTA's moments (read by the cluster)
   float k[kOdeD], a[kOdeD], sigma[kOdeD];
 };
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   __nv_bfloat16* vp_s = reinterpret_cast<__nv_bfloat16*>(ode_smem + sizeof(OdeShared));
   const int Tc = (T + kOdeCluster - 1) / kOdeCluster;
   __nv_bfloat16* r_s = vp_s + (size_t)Tc * kOdeD;
+  float* w_s = reinterpret_cast<float*>(r_s + (size_t)Tc * kOdeD);  // guidance - 1 of the CTA's rows
 
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
@@ -218,6 +222,8 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   }
 
   const bool cfg = (flags & DEMON_ODE_CFG) != 0;
+  if (cfg)  // the guidance curve of the CTA's rows, read by the moment pass and phase 2
+    for (int i = tid; i < t1 - t0; i += kOdeThreads) w_s[i] = rnd(curve(S.guidance, S.guidance_s, t0 + i)) - 1.0f;
   const bool mom_init = (flags & DEMON_ODE_MOM_INIT) != 0;
   const bool cache_neg = (flags & DEMON_ODE_CACHE_NEG) != 0;
   const int n_pos = S.n_pos, n_neg = S.n_neg;
@@ -271,7 +277,7 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
     for (int t = t0 + g; t < t1; t += 4) {
       const int64_t loc = (int64_t)(t - t0) * kOdeD;
       const float vp = __bfloat162float(vpc[loc]), r = __bfloat162float(rc[loc]);
-      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f, w2 = w * w;
+      const float w = w_s[t - t0], w2 = w * w;
       const float pp = vp * vp, pr = vp * r, rr2 = r * r;
       m0 += rr2;
       m1 += pp;
@@ -302,13 +308,21 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   }
   cluster.sync();  // partial moments of every CTA are visible cluster-wide
   if (cfg) {
-    if (tid < kOdeD) {
-      double tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int rnk = 0; rnk < kOdeCluster; ++rnk) {
-        const double* peer = cluster.map_shared_rank(&sh.cta_part[tid][0], rnk);
+    // the slot's 64 x 8 moments: two per thread, each summed over the 8 CTAs in rank order
+    // (the eight distributed-shared-memory loads of a sum are in flight together)
+    for (int e = tid; e < kOdeD * 8; e += kOdeThreads) {
+      const int cc = e >> 3, i = e & 7;
+      double part[kOdeCluster];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) tot[i] += peer[i];
-      }
+      for (int rnk = 0; rnk < kOdeCluster; ++rnk) part[rnk] = *cluster.map_shared_rank(&sh.cta_part[cc][i], rnk);
+      double acc = 0.0;
+#pragma unroll
+      for (int rnk = 0; rnk < kOdeCluster; ++rnk) acc += part[rnk];
+      sh.tot[cc][i] = acc;
+    }
+    __syncthreads();
+    if (tid < kOdeD) {
+      const double* tot = sh.tot[tid];
       const double Srr = tot[0], P0 = tot[1], Srp = tot[2], P1 = tot[3], P2 = tot[4], Q1 = tot[5], Q2 = tot[6],
                    R2 = tot[7];
       const double nr = sqrt(Srr);
@@ -361,7 +375,7 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
       const uint4 rv = lds16(r_s, loc);
       stg16(S.momentum, off, rv);
       words(rv, r);
-      const float w = rnd(curve(S.guidance, S.guidance_s, t)) - 1.0f;
+      const float w = w_s[t - t0];
       const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -490,7 +504,7 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   DEMON_CHECK_ARG(((uintptr_t)slots & 7) == 0, "ode: slot table must be 8-byte aligned");
   DEMON_CHECK_ARG(!gain || ((uintptr_t)gain & 15) == 0, "ode: gain must be 16-byte aligned");
   const int Tc = (int)((T + kOdeCluster - 1) / kOdeCluster);
-  const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16);
+  const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16) + (size_t)Tc * sizeof(float);
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {
     DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024));
