@@ -204,7 +204,8 @@ def ode_workload(dev, nslots=64, T=1500, seed=0):
     """Config-3 slot features at config-5 scale: 64 slots x T=1500 x 64, CFG modes cycling
     standard / RCFG-initialize (cached negative) / RCFG-self, per-slot guidance U(3,7),
     per-frame velocity_scale / sde_denoise / apg_momentum / cfg_rescale splines in [0, 1.5],
-    source latents (SDE-curve path), binary latent mask with 40 % spans, channel gain U(0.8, 1.2).
+    source latents (SDE-curve path), binary latent mask with 40 % spans, channel gain U(0.8, 1.2),
+    DCW double with the reference's default scalers (on by default in its DiffusionConfig).
     Returns (OdeTick with the slots added, algorithmic bytes per launch, gain)."""
     import torch
     from demon_b200 import ode
@@ -243,7 +244,7 @@ def ode_workload(dev, nslots=64, T=1500, seed=0):
             guidance=float(torch.rand(1, generator=g)) * 4 + 3, apg_momentum=spline(0, 1.5),
             cfg_rescale=spline(0, 1.5), velocity_scale=spline(0, 1.5), sde_denoise_curve=spline(0, 1.5),
             source=lat(), mask=ode.LatentMask(m.to(dev), lat(), lat()),
-            dec_out=torch.empty(T, D, dtype=bf, device=dev), seed=1000 + i)
+            dec_out=torch.empty(T, D, dtype=bf, device=dev), dcw=("double", 0.05, 0.02), seed=1000 + i)
         tick.add(st)
         # reads: v_pos, v_neg source, momentum, xt, mask original + noise, source, gain; writes: momentum, xt, dec
         nbytes += elems * 2 * (8 + 3)
@@ -724,7 +725,7 @@ def cpu_stream_sample(budget_s: float, layers: int = 2):
     slot = dict(xt=lat(), pos=[(lat(), None)], neg=[(lat(), None)], momentum=lat(), has_cfg=True,
                 rcfg_mode=None, guidance=np.full(T5, 5.0, np.float32), apg_momentum=-0.75, cfg_rescale=None,
                 velocity_scale=np.ones(T5, np.float32), t_curr=0.75, t_next=0.5, step_idx=3, total_steps=8,
-                infer_method="ode", noise=None, dec_next=True)
+                infer_method="ode", noise=None, dec_next=True, dcw=("double", 0.05, 0.02))
     t1 = time.perf_counter()
     nodes = 0
     try:

@@ -32,6 +32,9 @@ ODE_CACHE_NEG = 1 << 10
 ODE_DEC_OUT = 1 << 11
 ODE_DEC_MASK = 1 << 12
 ODE_VS = 1 << 13
+ODE_DCW_LO = 1 << 14
+ODE_DCW_HI = 1 << 15
+ODE_DCW_PIX = 1 << 16
 
 EXPORTED = (
     "demon_abi_version", "demon_struct_sizes", "demon_last_error", "demon_device_status",
@@ -78,6 +81,7 @@ class DemonOdeSlot(ctypes.Structure):
         ("noise", _vp), ("dec_out", _vp),
         ("mask_s_next", _f32), ("t_curr", _f32), ("t_next", _f32), ("flags", _i32),
         ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64),
+        ("dcw_lo", _vp), ("dcw_lo_s", _f32), ("dcw_hi", _vp), ("dcw_hi_s", _f32),
     ]
 
 

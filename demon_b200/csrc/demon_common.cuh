@@ -392,6 +392,11 @@ __device__ __forceinline__ float2 add_f2(float2 a, float2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return bits_f2(r);
 }
+__device__ __forceinline__ float2 sub_f2(float2 a, float2 b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(r);
+}
 // bf16x2 <-> float2 (exact widening; narrowing rounds to nearest even)
 __device__ __forceinline__ float2 bf2_f2(uint32_t v) {
   return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));

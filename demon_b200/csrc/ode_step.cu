@@ -50,6 +50,12 @@ constexpr int kOdeMaxT = 6400;
 
 __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Rows of a slot per CTA of its cluster: even, so the row pairs (2k, 2k+1) of the DCW wavelet
+// step never straddle two CTAs.
+__host__ __device__ __forceinline__ int ode_rows_per_cta(int T) {
+  return (T + 2 * kOdeCluster - 1) / (2 * kOdeCluster) * 2;
+}
+
 __device__ __forceinline__ void ld4(const void* p, int64_t off, float (&v)[4]) {
   const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + off);
   v[0] = bf16_lo(u.x);
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   OdeShared& sh = *reinterpret_cast<OdeShared*>(ode_smem);
   __shared__ __align__(16) DemonOdeSlot s_slot;
   __nv_bfloat16* vp_s = reinterpret_cast<__nv_bfloat16*>(ode_smem + sizeof(OdeShared));
-  const int Tc = (T + kOdeCluster - 1) / kOdeCluster;
+  const int Tc = ode_rows_per_cta(T);
   __nv_bfloat16* r_s = vp_s + (size_t)Tc * kOdeD;
   float* w_s = reinterpret_cast<float*>(r_s + (size_t)Tc * kOdeD);  // guidance - 1 of the CTA's rows
 
@@ -352,8 +358,14 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   const bool need_noise = !final_step && (sde_curve || (sde_bare && !mask) || (onc_on && !sde_bare));
   const bool noise_in = need_noise && S.noise != nullptr;
   const bool need_mask_data = mask || dec_mask;
+  const bool dcw_pix = (flags & DEMON_ODE_DCW_PIX) != 0;
+  const bool dcw_band = (flags & (DEMON_ODE_DCW_LO | DEMON_ODE_DCW_HI)) != 0;
 
-  for (int t = t0 + rr; t < t1; t += 32) {
+  // Every lane of a warp runs the same iterations (the DCW wavelet step exchanges adjacent rows
+  // between lanes): a lane past the CTA's rows computes row t1 - 1 and stores nothing.
+  for (int tb = t0; tb < t1; tb += 32) {
+    const bool act = tb + rr < t1;
+    const int t = act ? tb + rr : t1 - 1;
     const int64_t off = (int64_t)t * kOdeD + c0;
     const int64_t loc = (int64_t)(t - t0) * kOdeD + c0;
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -373,7 +385,7 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
     if (cfg) {  // v_g = v + w (k r - a v), then cfg_rescale; rounded once (apg_forward + cfg_rescale)
       uint32_t r[4];
       const uint4 rv = lds16(r_s, loc);
-      stg16(S.momentum, off, rv);
+      if (act) stg16(S.momentum, off, rv);
       words(rv, r);
       const float w = w_s[t - t0];
       const float rho = resc ? rnd(curve(S.rescale, S.rescale_s, t)) : 0.f;
@@ -474,8 +486,43 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
         }
       }
     }
-    stg16(S.xt, off, make_uint4(xn[0], xn[1], xn[2], xn[3]));
-    if (dec_out) {
+    if (dcw_pix || dcw_band) {
+      // DCW (StreamPipeline._maybe_dcw, stream.py:1387-1405): denoised = bf16(x - bf16(vt t_curr))
+      // from the mask-blended state and the guided velocity before velocity_scale
+      uint32_t den[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) den[j] = sub_bf2(x[j], scal_bf2(tc, vt[j]));
+      if (dcw_pix) {  // dcw_pix (dcw.py:164-174): bf16(x + bf16(s bf16(x - denoised)))
+        const uint32_t s2 = bf2_dup(rnd(curve(S.dcw_lo, S.dcw_lo_s, t)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xn[j] = add_bf2(xn[j], mul_bf2(s2, sub_bf2(xn[j], den[j])));
+      } else {
+        // dcw_low / dcw_high / dcw_double (dcw.py:190-234) in fp32: a single-level haar DWT
+        // along T of rows (2k, 2k+1), held by lanes l and l ^ 8 (a missing partner row is the
+        // zero padding of an odd T), xL += lo (xL - yL), xH += hi (xH - yH), inverse DWT; both
+        // lanes of a pair compute the bands and keep their own output row
+        const bool even = (t & 1) == 0, pact = tb + (rr ^ 1) < t1;
+        const int k = t >> 1;
+        const float2 lo = f2_dup((flags & DEMON_ODE_DCW_LO) ? curve(S.dcw_lo, S.dcw_lo_s, k) : 0.0f);
+        const float2 hi = f2_dup((flags & DEMON_ODE_DCW_HI) ? curve(S.dcw_hi, S.dcw_hi_s, k) : 0.0f);
+        const float2 R = f2_dup(0.70710678118654752f), zf = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t px = __shfl_xor_sync(0xffffffffu, xn[j], 8);
+          const uint32_t pd = __shfl_xor_sync(0xffffffffu, den[j], 8);
+          const float2 mx = bf2_f2(xn[j]), md = bf2_f2(den[j]);
+          const float2 ox = pact ? bf2_f2(px) : zf, od = pact ? bf2_f2(pd) : zf;
+          const float2 xa = even ? mx : ox, xb = even ? ox : mx, ya = even ? md : od, yb = even ? od : md;
+          float2 xl = mul_f2(add_f2(xa, xb), R), xh = mul_f2(sub_f2(xa, xb), R);
+          const float2 yl = mul_f2(add_f2(ya, yb), R), yh = mul_f2(sub_f2(ya, yb), R);
+          xl = add_f2(xl, mul_f2(lo, sub_f2(xl, yl)));
+          xh = add_f2(xh, mul_f2(hi, sub_f2(xh, yh)));
+          xn[j] = f2_bf2(mul_f2(even ? add_f2(xl, xh) : sub_f2(xl, xh), R));
+        }
+      }
+    }
+    if (act) stg16(S.xt, off, make_uint4(xn[0], xn[1], xn[2], xn[3]));
+    if (dec_out && act) {
       uint32_t d[4] = {xn[0], xn[1], xn[2], xn[3]};
       if (dec_mask) {  // mask_pre_blend at t_next with the next step's strength
         const float mn = rnd(__ldg(S.mask + t) * S.mask_s_next);
@@ -503,7 +550,7 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   DEMON_CHECK_ARG(n <= 65535 / kOdeCluster, "ode: too many slots (%d)", n);
   DEMON_CHECK_ARG(((uintptr_t)slots & 7) == 0, "ode: slot table must be 8-byte aligned");
   DEMON_CHECK_ARG(!gain || ((uintptr_t)gain & 15) == 0, "ode: gain must be 16-byte aligned");
-  const int Tc = (int)((T + kOdeCluster - 1) / kOdeCluster);
+  const int Tc = ode_rows_per_cta((int)T);
   const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16) + (size_t)Tc * sizeof(float);
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {

@@ -43,6 +43,23 @@ def _as_curve(v, T: int):
     return _bf16_round(t)
 
 
+def _norm_curve(v) -> torch.Tensor:
+    """normalize_curve (acestep/engine/ode_steps.py:36-64) on the host: a Python scalar -> fp32
+    [1, 1, 1]; a tensor keeps its dtype, reshaped to [1, 1, 1] / [1, T, 1] / [B, T, 1]."""
+    if isinstance(v, (int, float, bool)):
+        return torch.tensor([[[float(v)]]], dtype=torch.float32)
+    t = torch.as_tensor(v).detach().to("cpu")
+    if t.ndim == 0:
+        return t.reshape(1, 1, 1).to(torch.float32)
+    if t.ndim == 1:
+        return t.unsqueeze(0).unsqueeze(-1)
+    if t.ndim == 2:
+        return t.unsqueeze(-1)
+    if t.ndim == 3:
+        return t
+    raise ValueError(f"normalize_curve: expected scalar / 0-d / 1-d / 2-d / 3-d, got {t.ndim}-d")
+
+
 @dataclass
 class LatentMask:
     """Latent-noise mask of a slot (acestep/engine/masking.py:9-71): mask [T]
@@ -92,6 +109,7 @@ class SlotStep:
     infer_method: str = "ode"
     noise: Optional[torch.Tensor] = None           # explicit step noise (else in-kernel Philox)
     dec_out: Optional[torch.Tensor] = None         # next tick's decoder input row
+    dcw: Optional[tuple] = None                    # active DCW corrector: (mode, scaler, high_scaler)
     seed: int = 0
     keep: list = field(default_factory=list)
 
@@ -184,8 +202,8 @@ class OdeTick:
             raise ValueError("latent width must be 64")
         self.device = torch.device(device)
         self.T, self.D, self.max_slots = T, D, max_slots
-        # per slot: descriptor + up to 12 curves of T floats
-        self.capacity = max_slots * (self.SLOT_BYTES + 12 * 4 * T + 256)
+        # per slot: descriptor + up to 18 curves of T floats (weights, step curves, DCW bands)
+        self.capacity = max_slots * (self.SLOT_BYTES + 18 * (4 * T + 16) + 256)
         self._host = [torch.empty(self.capacity, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
         self._dev = [torch.empty(self.capacity, dtype=torch.uint8, device=self.device) for _ in range(2)]
         self._events = [None, None]
@@ -284,11 +302,51 @@ class OdeTick:
             d.noise = nat.ptr(s.noise)
             d.dec_out = nat.ptr(s.dec_out)
             d.t_curr, d.t_next = float(s.t_curr), float(s.t_next)
+            if s.dcw is not None:
+                flags |= self._stage_dcw(d, s, put_curve)
             d.flags = flags
             d.seed = int(s.seed) & ((1 << 64) - 1)
             d.step = int(s.step_idx)
         del table
         return b, off[0]
+
+    def _stage_dcw(self, d, s: SlotStep, put_curve) -> int:
+        """DCW coefficients of one slot: DCWCorrector.apply (acestep/engine/dcw.py:428-490) scales
+        the low band by t * scaler and the high band by (1 - t) * scaler (double: high_scaler),
+        resampled to the band length by _shape_for_wavelet (dcw.py:408-426); pix mode uses the
+        raw scaler per frame in the pipeline dtype.  Evaluated with the reference's own tensor
+        ops on the host."""
+        mode, sc, hsc = s.dcw
+        T, t = self.T, float(s.t_curr)
+        if mode == "pix":
+            c = _as_curve(sc, T)
+            d.dcw_lo, d.dcw_lo_s = put_curve(c), (c if isinstance(c, float) else 0.0)
+            return nat.ODE_DCW_PIX
+        if mode not in ("low", "high", "double"):
+            raise ValueError(f"invalid dcw mode {mode!r}")
+        Td = (T + 1) // 2
+
+        def band(coef, tm):
+            c = _norm_curve(coef)                              # [1, T, 1] or [1, 1, 1]
+            c = (tm * c).permute(0, 2, 1).contiguous().to(torch.float32)
+            if c.shape[-1] not in (1, T):
+                raise ValueError(f"DCW scaler curve has {c.shape[-1]} frames, expected 1 or T={T}")
+            if c.shape[-1] == 1:
+                return float(c.reshape(-1)[0])
+            if c.shape[-1] != Td:
+                c = torch.nn.functional.interpolate(c, size=Td, mode="linear", align_corners=False)
+            return c.reshape(-1).contiguous()
+
+        f = 0
+        if mode in ("low", "double"):
+            b = band(sc, t)
+            d.dcw_lo, d.dcw_lo_s = put_curve(b), (b if isinstance(b, float) else 0.0)
+            f |= nat.ODE_DCW_LO
+        if mode in ("high", "double"):
+            b = band(hsc if mode == "double" else sc, 1.0 - t)
+            d.dcw_hi, d.dcw_hi_s = put_curve(b), (b if isinstance(b, float) else 0.0)
+            f |= nat.ODE_DCW_HI
+        return f
 
     def _launch(self, fn, gain: Optional[torch.Tensor], stream) -> None:
         if not self.slots:

@@ -167,12 +167,44 @@ class GraphedDecoder:
 @dataclass
 class StreamConfig:
     """The DiffusionConfig fields the tick reads (acestep/engine/diffusion.py:13-59).
-    DCW (on by default in the reference, dcw.py:428-490) is not applied: the tick here is the
-    reference's tick with ``dcw_enabled=False``."""
+
+    DCW (Differential Correction in Wavelet domain, acestep/engine/dcw.py) is on by default
+    with the reference's defaults (diffusion.py:48-59) and runs inside the fused ODE kernel;
+    the haar wavelet is implemented (the reference's default), other wavelets and the
+    advanced faders (DCWAdvanced) raise NotImplementedError."""
     infer_steps: int = 8
     infer_method: str = "ode"
     shift: float = 3.0
     noise_on_cpu: bool = True
+    dcw_enabled: bool = True
+    dcw_mode: str = "double"
+    dcw_scaler: object = 0.05
+    dcw_high_scaler: object = 0.02
+    dcw_wavelet: str = "haar"
+    dcw_advanced: object = None
+
+
+DCW_MODES = ("low", "high", "double", "pix")
+
+
+def _dcw_spec(enabled: bool, mode: str, scaler, high_scaler, wavelet: str, advanced) -> Optional[tuple]:
+    """DCWCorrector construction (dcw.py:348-391): validates the mode and returns the
+    (mode, scaler, high_scaler) the kernel applies, or None when the corrector is inactive
+    (disabled, or every scaler it uses is zero)."""
+    if mode not in DCW_MODES:
+        raise ValueError(f"Invalid dcw_mode='{mode}'. Expected one of {DCW_MODES}.")
+    if not enabled:
+        return None
+    if wavelet != "haar":
+        raise NotImplementedError(f"DCW wavelet {wavelet!r}: only 'haar' is implemented")
+    if advanced is not None and any(float(getattr(advanced, f, 0.0)) > 0.0
+                                    for f in ("mult_blend", "mag_phase", "soft_thresh")):
+        raise NotImplementedError("DCW advanced faders (mult_blend / mag_phase / soft_thresh) are not implemented")
+
+    def nz(v):
+        return bool(torch.as_tensor(v, dtype=torch.float32).abs().gt(0).any())
+    active = nz(scaler) or (mode == "double" and nz(high_scaler))
+    return (mode, scaler, high_scaler) if active else None
 
 
 def build_schedule(steps: int, shift: float, denoise: float, dtype=torch.bfloat16) -> torch.Tensor:
@@ -228,6 +260,10 @@ class StreamPipeline:
         self._last_tick_ms = 0.0
         self._gain_dirty = False
         self._stage = [(None, None)] * 16   # pinned noise staging ring
+        cfg = self.config
+        self._dcw_cfg = dict(mode=cfg.dcw_mode, scaler=cfg.dcw_scaler, high_scaler=cfg.dcw_high_scaler,
+                             wavelet=cfg.dcw_wavelet, advanced=cfg.dcw_advanced)
+        self._dcw = _dcw_spec(cfg.dcw_enabled, **self._dcw_cfg)
         self._stage_i = 0
 
     # ------------------------------------------------------------------ properties
@@ -249,6 +285,17 @@ class StreamPipeline:
         if len(self._queue) >= self._depth:
             self._queue.pop(0)
         self._queue.append(request)
+
+    def set_dcw(self, *, enabled: bool, mode: Optional[str] = None, scaler=None, high_scaler=None,
+                wavelet: Optional[str] = None, advanced=None) -> None:
+        """stream.py:1357-1385: replace the DCW corrector; takes effect on the next tick."""
+        c = self._dcw_cfg
+        self._dcw_cfg = dict(mode=mode if mode is not None else c["mode"],
+                             scaler=scaler if scaler is not None else c["scaler"],
+                             high_scaler=high_scaler if high_scaler is not None else c["high_scaler"],
+                             wavelet=wavelet if wavelet is not None else c["wavelet"],
+                             advanced=advanced if advanced is not None else c["advanced"])
+        self._dcw = _dcw_spec(enabled, **self._dcw_cfg)
 
     def set_shared_curve(self, name: str, value) -> None:
         """stream.py:1319-1340: override a per-slot curve for every in-flight slot."""
@@ -456,7 +503,7 @@ class StreamPipeline:
             complex_extra=bool(req.extra_conditions or req.primary_temporal_weight is not None
                                or req.primary_step_range is not None),
             infer_method=self.config.infer_method,
-            dec_out=self._dec[si] if dec_next else None, seed=sl.seed)
+            dec_out=self._dec[si] if dec_next else None, dcw=self._dcw, seed=sl.seed)
         return st
 
     @torch.no_grad()

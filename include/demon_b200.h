@@ -242,7 +242,10 @@ enum {
   DEMON_ODE_CACHE_NEG = 1 << 10,  /* write v_neg into neg_cache (RCFG initialize, step 0) */
   DEMON_ODE_DEC_OUT = 1 << 11,    /* write next tick's decoder input */
   DEMON_ODE_DEC_MASK = 1 << 12,   /* next decoder input is mask-pre-blended */
-  DEMON_ODE_VS = 1 << 13          /* velocity_scale present */
+  DEMON_ODE_VS = 1 << 13,         /* velocity_scale present */
+  DEMON_ODE_DCW_LO = 1 << 14,     /* DCW: correct the haar low band (dcw_lo = t * scaler per band) */
+  DEMON_ODE_DCW_HI = 1 << 15,     /* DCW: correct the haar high band (dcw_hi = (1 - t) * scaler) */
+  DEMON_ODE_DCW_PIX = 1 << 16     /* DCW pix mode: x + s (x - denoised) per frame (s = dcw_lo) */
 };
 
 #define DEMON_ODE_MAX_COND 4
@@ -277,6 +280,12 @@ typedef struct DemonOdeSlot {
   int32_t flags;
   uint64_t seed;                               /* Philox key for in-kernel noise */
   uint64_t step;                               /* Philox counter offset (step index) */
+  /* DCW post-step correction (StreamPipeline._maybe_dcw, stream.py:1387-1405;
+   * DCWCorrector.apply, dcw.py:428-490): band coefficients per haar band k = t / 2
+   * ([ceil(T / 2)] fp32, the scaler curves already multiplied by t / (1 - t) and resampled),
+   * or per frame ([T]) in pix mode; NULL = the scalar next to it. */
+  const float* dcw_lo; float dcw_lo_s;
+  const float* dcw_hi; float dcw_hi_s;
 } DemonOdeSlot;
 
 /*

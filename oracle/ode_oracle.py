@@ -113,7 +113,8 @@ def step_slot(s: dict, rnd=bf16) -> dict:
     source, x0_target, x0_target_curve, x0_target_gate, x0_target_strength,
     mask: None or {mask [T], strength, strength_next, original, noise},
     complex_extra (extra_conditions / primary_temporal_weight / primary_step_range set),
-    noise: the step's randn draw [T, 64], gain: [T, 64] or None, dec_next (bool).
+    noise: the step's randn draw [T, 64], gain: [T, 64] or None, dec_next (bool),
+    dcw: None or (mode, scaler, high_scaler) of an active DCW corrector (see :func:`dcw`).
     """
     T = s["xt"].shape[0]
     x_state = np.asarray(s["xt"], np.float64)
@@ -194,16 +195,82 @@ def step_slot(s: dict, rnd=bf16) -> dict:
             vb = rnd(rnd(x - x0) / tc)                                   # stream.py:1269-1273
             xn = x + (tn - tc) * vb + eps * onc * tn
     xn = rnd(xn)
+    if s.get("dcw") is not None:                                         # _maybe_dcw (stream.py:1387-1405)
+        xn = dcw(xn, x, vt, tc, s["dcw"], rnd)
     out["xt"] = xn
     if s.get("dec_next"):
-        d = xn
-        if mask is not None:
-            mn = rnd(_curve(mask["mask"], T) * float(mask.get("strength_next", 1.0)))
-            d = pre_blend(xn, tn, mn, mask["noise"], mask["original"], rnd)
-        if s.get("gain") is not None:
-            d = rnd(d * np.asarray(s["gain"], np.float64))
-        out["dec"] = d
+        out["dec"] = next_dec(xn, s, rnd)
     return out
+
+
+def next_dec(xn, s: dict, rnd=bf16):
+    """The next tick's decoder input from the new state: mask_pre_blend at t_next with the
+    next step's strength, times the channel gain (stream.py:983-998 of the following tick)."""
+    T = xn.shape[0]
+    d = np.asarray(xn, np.float64)
+    mask = s.get("mask")
+    if mask is not None:
+        mn = rnd(_curve(mask["mask"], T) * float(mask.get("strength_next", 1.0)))
+        d = pre_blend(d, float(s["t_next"]), mn, mask["noise"], mask["original"], rnd)
+    if s.get("gain") is not None:
+        d = rnd(d * np.asarray(s["gain"], np.float64))
+    return d
+
+
+SQRT_HALF = 0.7071067811865476
+
+
+def _band_scale(coef, t_mult: float, T: int, Td: int) -> np.ndarray:
+    """DCWCorrector._shape_for_wavelet of ``t_mult * coef`` (acestep/engine/dcw.py:408-426):
+    a scalar or [T] curve resampled to the band length Td by linear interpolation with
+    align_corners=False (torch.nn.functional.interpolate)."""
+    f32 = np.float32
+    c = (f32(t_mult) * np.asarray(coef, np.float64).reshape(-1).astype(f32)).astype(f32)  # fp32 tensor ops
+    if c.size == 1:
+        return np.full(Td, float(c[0]))
+    n = c.size
+    # the source index in fp32 as the interpolation kernel computes it
+    scale = f32(n) / f32(Td)
+    src = np.maximum(scale * (np.arange(Td, dtype=f32) + f32(0.5)) - f32(0.5), f32(0.0)).astype(f32)
+    i0 = src.astype(np.int64)
+    i1 = np.minimum(i0 + 1, n - 1)
+    lam = (src - i0.astype(f32)).astype(f32)
+    return ((f32(1.0) - lam) * c[i0] + lam * c[i1]).astype(np.float64)
+
+
+def dcw(x_next, x_pre, vt, t_curr: float, cfg, rnd=bf16):
+    """DCW post-step correction (Yu et al., CVPR 2026), the reference's fast path:
+    StreamPipeline._maybe_dcw (stream.py:1387-1405) -> DCWCorrector.apply (dcw.py:428-490)
+    -> dcw_low / dcw_high / dcw_double / dcw_pix (dcw.py:164-234).
+
+    denoised = x_pre - vt * t_curr (bf16 ops); then, for the wavelet modes, a single-level
+    haar DWT along T of both latents (zero padding of an odd T, pytorch_wavelets
+    DWT1DForward(J=1, mode='zero', wave='haar')), xL += t s (xL - yL) and / or
+    xH += (1 - t) s_h (xH - yH), inverse DWT, trim to T, round.  ``cfg`` = (mode, scaler,
+    high_scaler) with scalers scalar or [T].  Restated from the haar transform's definition
+    (cA = (a + b)/sqrt 2, cD = (a - b)/sqrt 2 and its inverse): the sign convention of the
+    detail band cancels between analysis and synthesis.  pytorch_wavelets is not installed
+    here, so this restatement is not pinned to it."""
+    mode, sc, hsc = cfg
+    x_next = np.asarray(x_next, np.float64)
+    T = x_next.shape[0]
+    den = rnd(np.asarray(x_pre, np.float64) - rnd(np.asarray(vt, np.float64) * t_curr))
+    if mode == "pix":                                                     # dcw_pix (:164-174)
+        s = rnd(_curve(sc, T))
+        return rnd(x_next + rnd(s * rnd(x_next - den)))
+    Td = (T + 1) // 2
+    xp = np.zeros((2 * Td, x_next.shape[1]))
+    yp = np.zeros_like(xp)
+    xp[:T], yp[:T] = x_next, den
+    xl, xh = (xp[0::2] + xp[1::2]) * SQRT_HALF, (xp[0::2] - xp[1::2]) * SQRT_HALF
+    yl, yh = (yp[0::2] + yp[1::2]) * SQRT_HALF, (yp[0::2] - yp[1::2]) * SQRT_HALF
+    if mode in ("low", "double"):
+        xl = xl + _band_scale(sc, t_curr, T, Td)[:, None] * (xl - yl)
+    if mode in ("high", "double"):
+        xh = xh + _band_scale(hsc if mode == "double" else sc, 1.0 - t_curr, T, Td)[:, None] * (xh - yh)
+    out = np.empty_like(xp)
+    out[0::2], out[1::2] = (xl + xh) * SQRT_HALF, (xl - xh) * SQRT_HALF
+    return rnd(out[:T])
 
 
 def prepare_dec(s: dict, rnd=bf16):

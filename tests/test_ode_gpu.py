@@ -79,12 +79,19 @@ def make_spec(rng, T, kind):
         s["x0_target"] = bf(rng.standard_normal((T, D)))
         s["x0_target_strength"] = 0.375
         s["step_idx"] = 5
+    for mode in ("double", "low", "high", "pix"):
+        if "dcw" + mode in kind:
+            sc = rand_curve(rng, T, 0.0, 0.1).astype(np.float32) if "dcwcurve" in kind else 0.05
+            s["dcw"] = (mode, sc, 0.02)
     return s
 
 
 KINDS = ["plain", "vs", "vs+onc", "cfg", "cfg+curve+rescale", "cfg+fresh", "cfg+self+rescale", "cfg+init0+fresh",
          "cfg+cached+curve", "multi", "multi+cfg", "mask", "mask+cfg+curve", "x0curve", "x0scalar",
-         "sdecurve", "sdecurve+vs", "sdebare", "sdebare+mask", "mask+onc+vs"]
+         "sdecurve", "sdecurve+vs", "sdebare", "sdebare+mask", "mask+onc+vs",
+         # DCW post-step correction (haar bands, scalar or per-frame scalers; pix mode)
+         "dcwdouble", "cfg+vs+dcwdouble", "mask+cfg+dcwlow+dcwcurve", "sdecurve+dcwhigh", "x0scalar+dcwdouble+dcwcurve",
+         "cfg+dcwpix+dcwcurve", "mask+onc+vs+dcwdouble"]
 
 
 def to_slot(spec, dev, ode):
@@ -120,7 +127,7 @@ def to_slot(spec, dev, ode):
         x0_target_strength=_c(spec.get("x0_target_strength", 0.0)), mask=mask,
         complex_extra=spec.get("complex_extra", False), infer_method=spec.get("infer_method", "ode"),
         noise=t(spec["noise"]), dec_out=torch.zeros(T, D, dtype=torch.bfloat16, device=dev) if spec.get("dec_next") else None,
-        seed=1234)
+        dcw=(lambda d: None if d is None else (d[0], _c(d[1]), _c(d[2])))(spec.get("dcw")), seed=1234)
     return st
 
 
@@ -172,7 +179,11 @@ def test_ode_step_matches_oracle(cuda, T):
         if "neg_cache" in ref:
             assert np.array_equal(st.neg_cache_out.float().cpu().numpy(), ref["neg_cache"]), k
         if "dec" in ref:
-            check(f"{k}:dec", st.dec_out, ref["dec"], np.maximum(np.abs(ref["dec"]), scale))
+            # the decoder input from the kernel's own new state (the state is checked above; a
+            # one-ulp difference there would otherwise be amplified by the mask blend and gain)
+            xk = st.xt.float().cpu().numpy().astype(np.float64)
+            dref = OO.next_dec(xk, s, rnd=OO.bf16)
+            check(f"{k}:dec", st.dec_out, dref, np.maximum(np.abs(dref), scale))
 
 
 def test_ode_prepare_matches_oracle(cuda):

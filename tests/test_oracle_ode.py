@@ -59,3 +59,62 @@ def test_oracle_matches_reference_bf16(idx):
     assert np.mean(out["xt"] == ref) > 0.5, rec["key"]
     dec = OO.prepare_dec(s, rnd=OO.bf16)
     np.testing.assert_array_equal(dec, A["dec_in"])
+
+
+# ---------------------------------------------------------------------------------------
+# DCW post-step correction
+# ---------------------------------------------------------------------------------------
+
+def _dcw_records():
+    import json
+    from pathlib import Path
+    g = Path(__file__).resolve().parent / "golden"
+    meta = json.loads((g / "dcw_golden.json").read_text())["records"]
+    arrs = np.load(g / "dcw_golden.npz")
+
+    def val(a):
+        return (a.view(np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    out = []
+    for r in meta:
+        A = {n: val(arrs[f"{r['key']}/{n}"]) for n in ("x_next", "x_pre", "vt", "out")}
+        if r["curve"]:
+            A["scaler"] = arrs[f"{r['key']}/scaler"].astype(np.float64)
+            A["high_scaler"] = arrs[f"{r['key']}/high_scaler"].astype(np.float64)
+        out.append((r, A))
+    return out
+
+
+def test_dcw_oracle_matches_reference():
+    """oracle.dcw against the reference's DCWCorrector.apply (tests/golden/gen_dcw_golden.py):
+    bf16 outputs identical but for fp32-vs-fp64 ties, every element within one ulp."""
+    recs = _dcw_records()
+    assert {r["mode"] for r, _ in recs} == {"low", "high", "double", "pix"}
+    for r, A in recs:
+        sc = A["scaler"] if r["curve"] else r["scaler"]
+        hsc = A["high_scaler"] if r["curve"] else r["high_scaler"]
+        got = OO.dcw(A["x_next"], A["x_pre"], A["vt"], r["t_curr"], (r["mode"], sc, hsc), rnd=OO.bf16)
+        ref = A["out"]
+        scale = np.maximum(np.abs(ref), 2.0 ** -8)
+        ulp = 2.0 ** (np.floor(np.log2(scale)) - 7)
+        assert np.max(np.abs(got - ref) / ulp) <= 1.0, r
+        assert np.mean(got == ref) >= 0.99, (r, np.mean(got == ref))
+
+
+def test_dcw_zero_scalers_and_perfect_reconstruction():
+    rng = np.random.default_rng(3)
+    for T in (10, 11, 1):
+        x = OO.bf16(rng.standard_normal((T, 64)))
+        pre, vt = OO.bf16(rng.standard_normal((T, 64))), OO.bf16(rng.standard_normal((T, 64)))
+        for mode in ("low", "high", "double", "pix"):
+            assert np.array_equal(OO.dcw(x, pre, vt, 0.5, (mode, 0.0, 0.0)), x), (T, mode)
+
+
+def test_dcw_band_scale_matches_torch_interpolate():
+    import torch
+    for T in (1500, 751, 123, 10):
+        c = torch.rand(T, generator=torch.Generator().manual_seed(T))
+        Td = (T + 1) // 2
+        ref = torch.nn.functional.interpolate((0.375 * c).reshape(1, 1, T), size=Td, mode="linear",
+                                              align_corners=False).reshape(-1).double().numpy()
+        got = OO._band_scale(c.numpy(), 0.375, T, Td)
+        assert np.max(np.abs(got - ref)) <= 6e-8 * max(1.0, np.abs(ref).max())
