@@ -457,7 +457,9 @@ class StreamPipeline:
 
     def _forward(self, rows, slots):
         """One batched decoder call over (slot index, condition) rows (stream.py:605-663)."""
-        idx = torch.tensor([si for si, _ in rows], device=self._device)
+        # small host -> device inputs go through pinned memory: a pageable copy would make the
+        # host wait for the device (cudaMemcpyAsync from pageable memory synchronises the stream)
+        idx = torch.tensor([si for si, _ in rows], pin_memory=True).to(self._device, non_blocking=True)
         xb = self._dec.index_select(0, idx)
         mL = max(c.encoder_hidden_states.shape[1] for _, c in rows)
         enc = []
@@ -469,7 +471,7 @@ class StreamPipeline:
         enc = torch.cat(enc, 0)
         ctx = torch.cat([slots[si].ctx for si, _ in rows], 0)
         t = torch.tensor([float(slots[si].t_schedule[slots[si].step_idx]) for si, _ in rows],
-                         device=self._device, dtype=self._dtype)
+                         dtype=self._dtype, pin_memory=True).to(self._device, non_blocking=True)
         out = self.decoder(hidden_states=xb, timestep=t, timestep_r=t, attention_mask=None,
                            encoder_hidden_states=enc, encoder_attention_mask=None, context_latents=ctx,
                            use_cache=False, past_key_values=None)

@@ -3,7 +3,7 @@
 The ring's compute (StreamPipeline on a GPU) is replaced by a fake pipeline that finishes
 deterministic latents and records shared-curve updates, so the test covers exactly the
 multi-process part: slot ownership, curve broadcast tagged with the tick (applied on every
-rank at tag + 1) and the gather of finished latents to rank 0 in rank order.
+rank at tag + 2) and the gather of finished latents to rank 0 in rank order.
 """
 import os
 import socket
@@ -45,10 +45,12 @@ def _worker(rank, world, port, q):
         return {"velocity_scale": torch.full((T,), 1.0 + tick), "guidance_curve": None if tick % 8 else
                 torch.full((T,), 3.0 + tick)}
     gathered = []
-    for _ in range(10):
+    for _ in range(12):
         _, g = ring.step(src)
         if g is not None:
             gathered.append([float(x[0, 0, 0]) for x in g])
+    if rank == 0:
+        gathered.append([float(x[0, 0, 0]) for x in ring.collect()])
     q.put((rank, [ring.owns(i) for i in range(8)], pipe.curves, gathered))
     dist.barrier()
     dist.destroy_process_group()
@@ -79,13 +81,14 @@ def test_sharded_ring_two_ranks():
     # ownership: global slot g on rank g % 2
     assert res[0][0] == [g % 2 == 0 for g in range(8)]
     assert res[1][0] == [g % 2 == 1 for g in range(8)]
-    # curves broadcast at ticks 0, 4, 8 apply at ticks 1, 5, 9 on both ranks, identically
+    # curves broadcast at ticks 0, 4, 8 apply at ticks 2, 6, 10 on both ranks, identically
     assert res[0][1] == res[1][1]
     applied = {(t, n): v for t, n, v in res[0][1]}
-    assert applied[(1, "velocity_scale")] == 1.0 and applied[(1, "guidance_curve")] == 3.0
-    assert applied[(5, "velocity_scale")] == 5.0 and applied[(5, "guidance_curve")] is None
-    assert applied[(9, "velocity_scale")] == 9.0 and applied[(9, "guidance_curve")] == 11.0
-    assert sorted({t for t, _, _ in res[0][1]}) == [1, 5, 9]
-    # rank 0 gathers every finished latent, rank 0's first: tick t finishes on rank t % 2
+    assert applied[(2, "velocity_scale")] == 1.0 and applied[(2, "guidance_curve")] == 3.0
+    assert applied[(6, "velocity_scale")] == 5.0 and applied[(6, "guidance_curve")] is None
+    assert applied[(10, "velocity_scale")] == 9.0 and applied[(10, "guidance_curve")] == 11.0
+    assert sorted({t for t, _, _ in res[0][1]}) == [2, 6, 10]
+    # rank 0 gathers every finished latent, rank 0's first (tick t finishes on rank t % 2), each
+    # tick's set handed over at the next step (the first step returns the empty set before it)
     assert res[1][2] == []
-    assert res[0][2] == [[100.0 * (t % 2) + t] for t in range(10)]
+    assert res[0][2] == [[]] + [[100.0 * (t % 2) + t] for t in range(12)]
