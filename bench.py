@@ -129,7 +129,9 @@ def dist_init(world):
     import torch.distributed as dist
     if world > 1 and not dist.is_initialized():
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     return dist if world > 1 else None
 
 
