@@ -40,7 +40,7 @@ from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import nvfp4 as Q
 from .nvfp4 import NVFP4Linear
-from .rowops import adanorm_quantize, silu_mul_quantize
+from .rowops import adanorm_quantize, head_norm_rope, silu_mul_quantize
 
 try:  # FlashAttention 2 (library): unsplit KV loop via flash_attn_with_kvcache(num_splits=1)
     from flash_attn import flash_attn_with_kvcache as _fa_kvcache
@@ -156,6 +156,25 @@ def _has_lora(*lins) -> bool:
     return any(l.lora.active() is not None for l in lins)
 
 
+def _gemm_head_norm(a, w, hn, rope, **kw):
+    """NVFP4 GEMM whose first ``hn[0]`` output columns get the per-head RMSNorm (+ RoPE) of
+    q / k.  The GEMM epilogue does it when the output width is a multiple of 256 (a warp then
+    holds whole 128-column heads); otherwise the standalone head-norm kernel runs on the
+    output (the same arithmetic)."""
+    if hn is None or hn[0] == 0:
+        return Q.gemm(a, w, **kw)
+    if w.rows % 256 == 0:
+        return Q.gemm(a, w, head_norm=hn, rope=rope, **kw)
+    y = Q.gemm(a, w, **kw)
+    hn_cols, hn_q, wq, wk, eps = hn
+    rk = dict(cos=rope[0], sin=rope[1], S=rope[2]) if rope is not None else {}
+    if hn_q:
+        head_norm_rope(y, 0, hn_q // 128, wq, eps, **rk)
+    if hn_cols > hn_q:
+        head_norm_rope(y, hn_q, (hn_cols - hn_q) // 128, wk, eps, **rk)
+    return y
+
+
 class Attention(nn.Module):
     """AceStepAttention (turbo.py:263-378) with NVFP4 projections."""
 
@@ -202,12 +221,12 @@ class Attention(nn.Module):
             hn_cols = sum(l.out_features for l, sp in zip(lins, specs) if sp is not None)
             hn_q = sum(l.out_features for l in lins if l is self.q_proj)
             hn = (hn_cols, hn_q, self.q_norm.weight, self.k_norm.weight, self.q_norm.variance_epsilon)
-            return Q.gemm(a, self.fused() if len(lins) > 1 else _packed(lins[0]), head_norm=hn, rope=rope)
+            return _gemm_head_norm(a, self.fused() if len(lins) > 1 else _packed(lins[0]), hn, rope)
         outs = []
         for l in lins:
             xa, lb = _lora(l, xb, a)
             sp = self._norm_spec(l)
-            outs.append(Q.gemm(a, _packed(l), lora_xa=xa, lora_b=lb, head_norm=sp, rope=rope if sp else None))
+            outs.append(_gemm_head_norm(a, _packed(l), sp, rope if sp else None, lora_xa=xa, lora_b=lb))
         return torch.cat(outs, 1)
 
     def self_attn(self, a, xb, h, gate, B, S, rope):
@@ -228,7 +247,7 @@ class Attention(nn.Module):
     def cross_attn(self, a, xb, h, kv, B, S, L):
         hd, hq, hk = self.head_dim, self.hq, self.hk
         xa, lb = _lora(self.q_proj, xb, a)
-        q = Q.gemm(a, _packed(self.q_proj), lora_xa=xa, lora_b=lb, head_norm=self._norm_spec(self.q_proj))
+        q = _gemm_head_norm(a, _packed(self.q_proj), self._norm_spec(self.q_proj), None, lora_xa=xa, lora_b=lb)
         ld = kv.stride(0)
         k = kv.as_strided((B, L, hk, hd), (L * ld, ld, hd, 1))
         v = kv.as_strided((B, L, hk, hd), (L * ld, ld, hd, 1), hk * hd)

@@ -221,7 +221,11 @@ class LoRABank:
     alpha / rank factor, exactly the reference's delta
     (acestep/engine/lora.py:316-319) and writeback (lora.py:824-833).  The
     strength of each LoRA is a per-rank-column scale of the down projection,
-    so enable / disable / set_strength never touch the packed weight.
+    so enable / disable / set_strength never touch the packed weight.  A strength change
+    between two non-zero values rewrites that LoRA's segment of the device scale vector in
+    place (stream-ordered), so captured CUDA graphs stay valid and the change costs one small
+    fill at the next tick; adding, removing, enabling or zeroing a LoRA changes the
+    concatenated operands and bumps the weights generation.
     """
     entries: dict = field(default_factory=dict)
     _cat: tuple | None = None
@@ -238,7 +242,18 @@ class LoRABank:
         bump_generation()
 
     def set_strength(self, lora_id: str, strength: float) -> None:
-        self.entries[lora_id].strength = float(strength)
+        e = self.entries[lora_id]
+        old, new = e.strength, float(strength)
+        e.strength = new
+        if self._cat is not None and self._cat[0] is not None and e.enabled and old != 0.0 and new != 0.0:
+            off = 0
+            for x in self.entries.values():
+                if x is e:
+                    break
+                if x.enabled and x.strength != 0.0:
+                    off += x.A.shape[0]
+            self._cat[2][off:off + e.A.shape[0]].fill_(new)   # same operands: graphs stay valid
+            return
         self._cat = None
         bump_generation()
 

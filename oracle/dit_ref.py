@@ -17,6 +17,13 @@ replaces every linear the reference's FP8 export quantises (all but ``time_embed
 acestep/engine/trt/fp8_onnx.py:101-104) by the NVFP4 fake-quant of the C oracle:
 activation per-row quantise -> dequantise, weight per-tensor quantise -> dequantise,
 fp32 matmul, + bias, rounded to bf16.
+
+``lora`` ({linear name: [(A [r, K], B [N, r], strength), ...]}) adds hot LoRA deltas the way
+the reference's writeback defines them, ``W + sum_i s_i B_i A_i`` with raw ``B @ A``
+(acestep/engine/lora.py:316-319, 824-833): with ``fake_quant`` the base weight stays the
+NVFP4 fake-quant of W and the delta ``x (s B A)^T`` is added in fp32 from the bf16 input
+(the merged-weight comparison of a hot-LoRA epilogue); without it the bf16 weight is merged
+in fp32 and rounded to bf16, as the eager writeback ``param.add_(delta, alpha=s)`` does.
 """
 from __future__ import annotations
 
@@ -35,7 +42,15 @@ def _fq_weight(W: torch.Tensor) -> torch.Tensor:
 
 
 class DiTRef:
-    def __init__(self, state: dict, cfg: dict, fake_quant: bool = False):
+    def __init__(self, state: dict, cfg: dict, fake_quant: bool = False, lora: dict | None = None):
+        self.lora = dict(lora or {})
+        if not fake_quant and self.lora:
+            state = dict(state)
+            for name, entries in self.lora.items():
+                W = state[name + ".weight"].double()
+                for A, B, s in entries:
+                    W = W + s * (B.double() @ A.double())
+                state[name + ".weight"] = W.to(state[name + ".weight"].dtype)
         self.sd = state
         self.cfg = dict(cfg)
         self.fake_quant = fake_quant
@@ -62,6 +77,8 @@ class DiTRef:
         xb = x.reshape(-1, shp[-1]).to(torch.bfloat16).contiguous()
         ac, _, asl, ag = NO.quantize(xb.view(torch.int16).numpy().view(np.uint16), NO.GS_PER_ROW)
         y = torch.from_numpy(NO.dequantize(ac, asl, ag)) @ self._wq[name].t()
+        for A, B, s in self.lora.get(name, ()):
+            y = y + s * ((xb.double() @ A.double().t()) @ B.double().t()).float()
         if b is not None:
             y = y + b.float()
         return y.to(torch.bfloat16).reshape(*shp[:-1], -1)

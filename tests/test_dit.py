@@ -136,3 +136,93 @@ def test_attention_batch_invariant_at_dit_shapes(cuda):
             q[:2].transpose(1, 2).float(), kk[:2].transpose(1, 2).float(), vv[:2].transpose(1, 2).float(),
             attn_mask=mask, enable_gqa=True).transpose(1, 2)
         assert _rel(full[:2], ref) < 1e-2
+
+
+# ---------------------------------------------------------------------------------------
+# Hot LoRA in the decoder (rank 64 on every attention q/k/v/o and MLP
+# linear, strength swept, one enable / remove cycle)
+# ---------------------------------------------------------------------------------------
+
+def _lora_targets(n_layers):
+    out = []
+    for i in range(n_layers):
+        p = f"layers.{i}"
+        out += [f"{p}.self_attn.{n}_proj" for n in "qkvo"]
+        out += [f"{p}.cross_attn.{n}_proj" for n in "qkvo"]
+        out += [f"{p}.mlp.{n}_proj" for n in ("gate", "up", "down")]
+    return out
+
+
+def _lora_weights(m, rank, seed, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    lora = {}
+    for name in _lora_targets(len(m.layers)):
+        lin = m.get_submodule(name)
+        A = (torch.randn(rank, lin.in_features, generator=g) * std).to(torch.bfloat16)
+        B = (torch.randn(lin.out_features, rank, generator=g) * std).to(torch.bfloat16)
+        lora[name] = (A, B)
+    return lora
+
+
+@pytest.mark.gpu
+def test_dit_hot_lora_layers_match_merged_weights(cuda):
+    """Each layer with rank-64 hot LoRAs on all its attention and MLP linears, fed the
+    reference's layer inputs, against the oracle layer whose linears add the merged delta
+    s * B @ A exactly (lora.py:316-319, 824-833) to the fake-quant NVFP4 base."""
+    from demon_b200 import nvfp4 as Q
+    from oracle.dit_ref import DiTRef
+    d = _fixture()
+    m = _model(d, cuda)
+    lora = _lora_weights(m, 64, 41, std=0.04)   # a delta well above the layer tolerance
+    s = 0.75
+    for name, (A, B) in lora.items():
+        m.get_submodule(name).lora.set("cfg4", A.to(cuda), B.to(cuda), strength=s)
+    ref = DiTRef(make_state(d["shapes"]), d["cfg"], fake_quant=True,
+                 lora={n: [(A, B, s)] for n, (A, B) in lora.items()})
+    for i, rec in enumerate(d["layers"]):
+        B_, S, D = rec["h_in"].shape
+        L = rec["enc"].shape[1]
+        layer = m.layers[i]
+        enc = rec["enc"].to(cuda).reshape(B_ * L, D).contiguous()
+        kv = layer.cross_attn.cross_kv(Q.quantize(enc), enc, B_, L)
+        with torch.no_grad():
+            h = layer(rec["h_in"].to(cuda).reshape(B_ * S, D).contiguous(), rec["tproj"].to(cuda), kv, B_, S, L,
+                      m._rope(S, cuda, torch.bfloat16))
+        dt = torch.bfloat16
+        window = ref.window if (i + 1) % 2 else None
+        with torch.no_grad():
+            want = ref.layer(i, rec["h_in"], rec["tproj"], rec["enc"], ref.rope(S, dt), ref.mask4d(S, dt, window),
+                             ref.mask4d(max(S, L), dt, None)[:, :, :S, :L])
+        out, want, hin = h.view(B_, S, D).float().cpu(), want.float(), rec["h_in"].float()
+        upd_err = float((out - want).norm() / (want - hin).norm())
+        assert upd_err < 0.15, (i, upd_err)
+        assert _rel(out, want) < 0.08, i
+        # the LoRA moved the layer by more than twice that tolerance
+        assert float((want - rec["h_out"].float()).norm() / (rec["h_out"].float() - hin).norm()) > 0.3, i
+
+
+@pytest.mark.gpu
+def test_dit_hot_lora_strength_sweep_and_remove(cuda):
+    """Strength 0 is a no-op, every strength change takes effect on the next (graph-replayed)
+    forward without a weight rewrite, and removing the LoRAs restores the base bits."""
+    from demon_b200.stream import GraphedDecoder
+    d = _fixture()
+    m = _model(d, cuda)
+    g = GraphedDecoder(m)
+    base = _run(m, d, cuda)
+    assert torch.equal(_run(g, d, cuda), base)
+    lora = _lora_weights(m, 64, 43)
+    for name, (A, B) in lora.items():
+        m.get_submodule(name).lora.set("cfg4", A.to(cuda), B.to(cuda), strength=0.0)
+    assert torch.equal(_run(g, d, cuda), base)           # strength 0 contributes nothing
+    prev = base
+    for s in (0.25, 0.5, 1.0):
+        for name in lora:
+            m.get_submodule(name).lora.set_strength("cfg4", s)
+        eager, graphed = _run(m, d, cuda), _run(g, d, cuda)
+        assert torch.equal(graphed, eager), s             # the replayed graph follows the change
+        assert not torch.equal(eager, prev), s
+        prev = eager
+    for name in lora:
+        m.get_submodule(name).lora.remove("cfg4")
+    assert torch.equal(_run(g, d, cuda), base)
