@@ -602,6 +602,74 @@ class Ring:
         return fin
 
 
+def run_config3(dit, dev, ticks=24, warmup=24):
+    """BASELINE config 3 on one GPU: a depth-8 ring at T=750 (375 tokens) on the full DiT with
+    heterogeneous slots -- denoise cycling 1.0 / 0.5 / 0.75 (source latents), CFG cycling
+    standard / RCFG-initialize / RCFG-self, guidance U(3, 7), velocity_scale / sde_denoise /
+    apg_momentum / cfg_rescale as [750] splines in [0, 1.5], binary latent mask with 40 %
+    spans, channel gain U(0.8, 1.2), DCW on (the reference's default); one request submitted
+    per tick, one slot finished per tick (StreamPipeline.tick).  The rows per forward vary with
+    the CFG modes, so the warm-up runs long enough to capture every shape's graph before the
+    timed ticks.  Returns ticks/s (CUDA events)."""
+    import torch
+    from demon_b200.stream import (LatentNoiseMask, SlotCondition, SlotRequest, StreamConfig,
+                                   StreamPipeline)
+    T, L, D = 750, L5, 2048
+    g = torch.Generator().manual_seed(33)
+    bf = torch.bfloat16
+
+    def spline(lo, hi):
+        knots = torch.rand(16, generator=g) * (hi - lo) + lo
+        xs = torch.linspace(0, 15, T)
+        i = xs.floor().clamp(max=14).long()
+        f = xs - i
+        return knots[i] * (1 - f) + knots[i + 1] * f
+
+    ones = torch.ones(1, L, dtype=bf, device=dev)
+    reqs = []
+    for k in range(12):
+        src = torch.randn(1, T, 64, generator=g).to(bf).to(dev)
+        m = torch.zeros(T)
+        a0 = int(torch.randint(0, T - int(0.4 * T), (1,), generator=g))
+        m[a0:a0 + int(0.4 * T)] = 1.0
+        mode = ("standard", "initialize", "self")[k % 3]
+        kw = dict(guidance_curve=torch.tensor(float(torch.rand(1, generator=g)) * 4 + 3),
+                  velocity_scale=spline(0, 1.5), sde_denoise_curve=spline(0, 1.5),
+                  apg_momentum=spline(0, 1.5), cfg_rescale_curve=spline(0, 1.5))
+        if mode != "self":
+            kw["neg_conditions"] = [SlotCondition(torch.randn(1, L, D, generator=g).to(bf).to(dev), ones)]
+        if mode != "standard":
+            kw["rcfg_mode"] = mode
+        reqs.append(SlotRequest(
+            encoder_hidden_states=torch.randn(1, L, D, generator=g).to(bf).to(dev), encoder_attention_mask=ones,
+            context_latents=torch.randn(1, T, 128, generator=g).to(bf).to(dev), seed=700 + k,
+            source_latents=src, denoise=(1.0, 0.5, 0.75)[k % 3],
+            latent_mask=LatentNoiseMask(mask=m.to(dev), original_latents=src,
+                                        noise=torch.randn(1, T, 64, generator=g).to(bf).to(dev)), **kw))
+    pipe = StreamPipeline(dit, StreamConfig(infer_steps=8), pipeline_depth=8, device=dev, use_graphs=True)
+    pipe.set_channel_gain_tensor((torch.rand(1, T, 64, generator=g) * 0.4 + 0.8).to(bf).to(dev))
+    n = 0
+    for _ in range(8 + warmup):
+        pipe.submit(reqs[n % len(reqs)])
+        n += 1
+        pipe.tick()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(ticks):
+        pipe.submit(reqs[n % len(reqs)])
+        n += 1
+        pipe.tick()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / ticks
+    pipe.close()
+    return {"workload": "configs[2]: depth-8 ring, T=750 (375 tokens), 8 steps, heterogeneous slots "
+                        "(denoise 1.0/0.5/0.75, standard / RCFG-initialize / RCFG-self CFG, guidance U(3,7), "
+                        "four [750] spline curves, 40 % latent mask, channel gain, DCW), full DiT",
+            "value": 1e3 / ms, "unit": "ticks/s", "ms_per_tick": ms, "ticks": ticks}
+
+
 def gemm_roofline(dit, dev, B):
     """Device time of every NVFP4 GEMM of one eager DiT forward at batch B (CUDA events around
     each launch on the launching stream): algorithmic FLOPs / summed GEMM time."""
@@ -808,6 +876,7 @@ def run_stream(args):
         quant = measure_quantize_big(dev, stream)
         odek = measure_ode(dev, stream) if args.ode else None
         lin = linear_leg(dev, stream)
+        cfg3 = run_config3(dit, dev) if world == 1 else None
         cpu = None
         if world == 1 and args.cpu_seconds > 0:
             c = cpu_stream_sample(args.cpu_seconds)
@@ -853,6 +922,8 @@ def run_stream(args):
         }
         if odek is not None:
             line["kernels"]["ode_step"] = dict(odek, peak=pk["hbm_gbs"], frac=odek["achieved"] / pk["hbm_gbs"])
+        if cfg3 is not None:
+            line["secondary"] = {"config3_stream": cfg3}
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
