@@ -14,7 +14,7 @@
 //
 // APG and cfg_rescale reduce over T for each (slot, channel) (dims=(1,), the
 // reference's default, ode_steps.py:328-336 and :365-370).  The T axis of a
-// slot is split over an 8-CTA thread-block cluster; each CTA keeps its rows of
+// slot is split over a 4- or 8-CTA thread-block cluster; each CTA keeps its rows of
 // v_pos and of the new momentum in shared memory, accumulates per-channel
 // moments, and the cluster exchanges the partial moments through distributed
 // shared memory.  Every input byte is read from HBM once.
@@ -43,7 +43,8 @@ namespace cg = cooperative_groups;
 
 namespace demon {
 
-constexpr int kOdeCluster = 8;
+// CTAs per slot cluster: 8, or 4 when 8 would need a second wave of CTAs (see launch_ode)
+constexpr int kOdeClusterMax = 8;
 constexpr int kOdeThreads = 256;
 constexpr int kOdeD = 64;
 constexpr int kOdeMaxT = 6400;
@@ -52,8 +53,8 @@ __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2
 
 // Rows of a slot per CTA of its cluster: even, so the row pairs (2k, 2k+1) of the DCW wavelet
 // step never straddle two CTAs.
-__host__ __device__ __forceinline__ int ode_rows_per_cta(int T) {
-  return (T + 2 * kOdeCluster - 1) / (2 * kOdeCluster) * 2;
+__host__ __device__ __forceinline__ int ode_rows_per_cta(int T, int cluster) {
+  return (T + 2 * cluster - 1) / (2 * cluster) * 2;
 }
 
 __device__ __forceinline__ void ld4(const void* p, int64_t off, float (&v)[4]) {
@@ -173,23 +174,24 @@ __device__ __forceinline__ void words(uint4 v, uint32_t (&w)[4]) {
   w[3] = v.w;
 }
 
-// Layout: a slot's T rows are split over an 8-CTA cluster.  Row passes: thread = (row r in
+// Layout: a slot's T rows are split over a CL-CTA cluster.  Row passes: thread = (row r in
 // [0, 32), channel octet q in [0, 8)) with 16-byte loads; the moment pass: thread = (channel c,
 // row group g in [0, 4)) over the rows staged in shared memory.
-__global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
+template <int CL>
+__global__ void __launch_bounds__(kOdeThreads, CL == 8 ? 3 : 2) ode_step_kernel(const DemonOdeSlot* __restrict__ slots, int T,
                                                                const __nv_bfloat16* __restrict__ gain,
                                                                int prepare_only) {
   extern __shared__ __align__(16) uint8_t ode_smem[];
   OdeShared& sh = *reinterpret_cast<OdeShared*>(ode_smem);
   __shared__ __align__(16) DemonOdeSlot s_slot;
   __nv_bfloat16* vp_s = reinterpret_cast<__nv_bfloat16*>(ode_smem + sizeof(OdeShared));
-  const int Tc = ode_rows_per_cta(T);
+  const int Tc = ode_rows_per_cta(T, CL);
   __nv_bfloat16* r_s = vp_s + (size_t)Tc * kOdeD;
   float* w_s = reinterpret_cast<float*>(r_s + (size_t)Tc * kOdeD);  // guidance - 1 of the CTA's rows
 
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
-  const int slot_id = blockIdx.x / kOdeCluster;
+  const int slot_id = blockIdx.x / CL;
   const int tid = threadIdx.x;
   const int rr = tid >> 3, c0 = (tid & 7) * 8;  // row in pass, first channel of the octet
   {  // the slot descriptor, once per CTA, into shared memory
@@ -314,16 +316,16 @@ __global__ void __launch_bounds__(kOdeThreads, 3) ode_step_kernel(const DemonOde
   }
   cluster.sync();  // partial moments of every CTA are visible cluster-wide
   if (cfg) {
-    // the slot's 64 x 8 moments: two per thread, each summed over the 8 CTAs in rank order
-    // (the eight distributed-shared-memory loads of a sum are in flight together)
+    // the slot's 64 x 8 moments: two per thread, each summed over the CL CTAs in rank order
+    // (the distributed-shared-memory loads of a sum are in flight together)
     for (int e = tid; e < kOdeD * 8; e += kOdeThreads) {
       const int cc = e >> 3, i = e & 7;
-      double part[kOdeCluster];
+      double part[CL];
 #pragma unroll
-      for (int rnk = 0; rnk < kOdeCluster; ++rnk) part[rnk] = *cluster.map_shared_rank(&sh.cta_part[cc][i], rnk);
+      for (int rnk = 0; rnk < CL; ++rnk) part[rnk] = *cluster.map_shared_rank(&sh.cta_part[cc][i], rnk);
       double acc = 0.0;
 #pragma unroll
-      for (int rnk = 0; rnk < kOdeCluster; ++rnk) acc += part[rnk];
+      for (int rnk = 0; rnk < CL; ++rnk) acc += part[rnk];
       sh.tot[cc][i] = acc;
     }
     __syncthreads();
@@ -547,30 +549,47 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   DEMON_CHECK_ARG(slots != nullptr && n > 0, "ode: need a device slot table and n_slots > 0");
   DEMON_CHECK_ARG(D == kOdeD, "ode: latent width must be 64 (D=%lld)", (long long)D);
   DEMON_CHECK_ARG(T > 0 && T <= kOdeMaxT, "ode: 0 < T <= %d required (T=%lld)", kOdeMaxT, (long long)T);
-  DEMON_CHECK_ARG(n <= 65535 / kOdeCluster, "ode: too many slots (%d)", n);
+  DEMON_CHECK_ARG(n <= 65535 / kOdeClusterMax, "ode: too many slots (%d)", n);
   DEMON_CHECK_ARG(((uintptr_t)slots & 7) == 0, "ode: slot table must be 8-byte aligned");
   DEMON_CHECK_ARG(!gain || ((uintptr_t)gain & 15) == 0, "ode: gain must be 16-byte aligned");
-  const int Tc = ode_rows_per_cta((int)T);
-  const size_t smem = sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16) + (size_t)Tc * sizeof(float);
+  constexpr size_t kMaxSmem = 227 * 1024 - 1024;
+  auto smem_for = [&](int cluster) {
+    const int Tc = ode_rows_per_cta((int)T, cluster);
+    return sizeof(OdeShared) + (size_t)Tc * kOdeD * 2 * sizeof(__nv_bfloat16) + (size_t)Tc * sizeof(float);
+  };
   static std::atomic<uint64_t> attr_done{0};
+  static int sms = 0;
   if (device_pending(attr_done)) {
-    DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024));
+    DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem));
+    DEMON_CUDA(cudaFuncSetAttribute(ode_step_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem));
+    int dev = 0;
+    DEMON_CUDA(cudaGetDevice(&dev));
+    DEMON_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     mark_device_done(attr_done);
   }
+  // 8-CTA clusters run 3 CTAs per SM; when that needs a second wave and 4-CTA clusters (2 per
+  // SM, twice the rows each) fit in one, the 4-CTA form is faster (64 slots x T=1500: 81 -> 69 us)
+  const int s = sms > 0 ? sms : 148;
+  const int cl = ((int64_t)n * 8 > 3LL * s && (int64_t)n * 4 <= 2LL * s && smem_for(4) <= kMaxSmem) ? 4 : 8;
+  const size_t smem = smem_for(cl);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(n * kOdeCluster));
+  cfg.gridDim = dim3((unsigned)(n * cl));
   cfg.blockDim = dim3(kOdeThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kOdeCluster;
+  attr[0].val.clusterDim.x = (unsigned)cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel, slots, (int)T,
-                                reinterpret_cast<const __nv_bfloat16*>(gain), prepare_only));
+  if (cl == 4)
+    DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<4>, slots, (int)T,
+                                  reinterpret_cast<const __nv_bfloat16*>(gain), prepare_only));
+  else
+    DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<8>, slots, (int)T,
+                                  reinterpret_cast<const __nv_bfloat16*>(gain), prepare_only));
   return DEMON_OK;
 }
 

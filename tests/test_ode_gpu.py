@@ -151,11 +151,15 @@ def check(name, got, ref, scale):
     assert exact >= 0.99, (name, exact)
 
 
-@pytest.mark.parametrize("T", [750, 123, 1500])
-def test_ode_step_matches_oracle(cuda, T):
+@pytest.mark.parametrize("T,n", [(750, None), (123, None), (1500, None), (301, 64)])
+def test_ode_step_matches_oracle(cuda, T, n):
+    """Every kind of slot once (n None), or n slots cycling through the kinds: 64 slots on a
+    148-SM B200 take the launch form with 4-CTA clusters (8-CTA clusters would need a second
+    wave of CTAs), fewer take 8-CTA clusters."""
     from demon_b200 import ode
     rng = np.random.default_rng(T)
-    specs = [make_spec(rng, T, k) for k in KINDS]
+    kinds = KINDS if n is None else [KINDS[i % len(KINDS)] for i in range(n)]
+    specs = [make_spec(rng, T, k) for k in kinds]
     gain = bf(rng.uniform(0.8, 1.2, (T, D)))
     for s in specs:
         s["gain"] = gain
@@ -168,7 +172,7 @@ def test_ode_step_matches_oracle(cuda, T):
     torch.cuda.synchronize()
     from demon_b200 import _native
     assert _native.device_status() == (0, 0)
-    for k, s, st in zip(KINDS, specs, slots):
+    for k, s, st in zip(kinds, specs, slots):
         ref = OO.step_slot(s, rnd=OO.bf16)
         scale = np.maximum(np.abs(ref["xt"]), np.abs(s["xt"]))
         check(f"{k}:xt", st.xt, ref["xt"], scale)
@@ -186,13 +190,14 @@ def test_ode_step_matches_oracle(cuda, T):
             check(f"{k}:dec", st.dec_out, dref, np.maximum(np.abs(dref), scale))
 
 
-def test_ode_prepare_matches_oracle(cuda):
+@pytest.mark.parametrize("n", [2, 64])
+def test_ode_prepare_matches_oracle(cuda, n):
     from demon_b200 import ode
     T = 300
     rng = np.random.default_rng(7)
     gain = bf(rng.uniform(0.8, 1.2, (T, D)))
-    specs = [make_spec(rng, T, k) for k in ("plain", "mask")]
-    tick = ode.OdeTick(cuda, T, max_slots=2)
+    specs = [make_spec(rng, T, ("plain", "mask")[i % 2]) for i in range(n)]
+    tick = ode.OdeTick(cuda, T, max_slots=n)
     slots = []
     for s in specs:
         s["gain"] = gain
