@@ -248,13 +248,14 @@ def ode_workload(dev, nslots=64, T=1500, seed=0):
             source=lat(), mask=ode.LatentMask(m.to(dev), lat(), lat()),
             dec_out=torch.empty(T, D, dtype=bf, device=dev), dcw=("double", 0.05, 0.02), seed=1000 + i)
         tick.add(st)
-        # reads: v_pos, v_neg source, momentum, xt, mask original + noise, source, gain; writes: momentum, xt, dec
-        nbytes += elems * 2 * (8 + 3)
+        # reads: v_pos, v_neg source, momentum, xt, mask original + noise, source; writes: momentum, xt, dec
+        nbytes += elems * 2 * (7 + 3)
+    nbytes += elems * 2  # the channel gain, shared by every slot
     return tick, nbytes, gain
 
 
 def measure_ode(dev, stream, reps=20):
-    """HBM roofline of the fused ODE step: two slot sets (2 x 135 MB > 2x L2) alternated."""
+    """HBM roofline of the fused ODE step: two slot sets (2 x 123 MB > 2x L2) alternated."""
     import torch
     from demon_b200 import _native as nat
     ticks = [ode_workload(dev, seed=s) for s in (0, 1)]

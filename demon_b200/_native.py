@@ -39,7 +39,8 @@ ODE_DCW_PIX = 1 << 16
 EXPORTED = (
     "demon_abi_version", "demon_struct_sizes", "demon_last_error", "demon_device_status",
     "demon_nvfp4_sf_bytes", "demon_nvfp4_quantize", "demon_nvfp4_gemm", "demon_lora_down",
-    "demon_ode_step", "demon_ode_prepare", "demon_nvfp4_noalloc_scratch_bytes", "demon_nvfp4_linear_noalloc",
+    "demon_ode_step", "demon_ode_prepare", "demon_ode_cluster_size", "demon_nvfp4_noalloc_scratch_bytes",
+    "demon_nvfp4_linear_noalloc",
     "demon_bf16_linear", "demon_adanorm_quantize", "demon_silu_mul_quantize", "demon_head_norm_rope",
 )
 
@@ -121,6 +122,7 @@ def load() -> ctypes.CDLL:
         L.demon_lora_down.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, ctypes.c_int, _vp, _vp, _vp]
         L.demon_ode_step.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
         L.demon_ode_prepare.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
+        L.demon_ode_cluster_size.argtypes = [_i32, _i64, ctypes.POINTER(_i32)]
         L.demon_nvfp4_linear_noalloc.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp]
         L.demon_bf16_linear.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp]
         L.demon_adanorm_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp,
@@ -167,6 +169,13 @@ def device_status(stream=None) -> tuple[int, int]:
     out = (ctypes.c_uint * 2)()
     check(load().demon_device_status(out, stream_ptr(stream)))
     return int(out[0]), int(out[1])
+
+
+def ode_cluster_size(n_slots: int, T: int) -> int:
+    """CTAs per slot cluster that the ODE launches use for n_slots x T on the current device."""
+    out = _i32()
+    check(load().demon_ode_cluster_size(n_slots, T, ctypes.byref(out)))
+    return out.value
 
 
 def sf_bytes(rows: int, K: int) -> int:

@@ -146,24 +146,42 @@ __global__ void __launch_bounds__(256) adanorm_quant_kernel(const NormArgs a) {
 }
 
 // The same row operation in the quantiser's geometry at D = 2048: one warp per row (4 blocks
-// of 16 per lane, 8 rows per CTA), so both row reductions are warp shuffles with no shared-
-// memory round trip, and the norm weight and the (at most two) modulation rows of the CTA's
-// 8 rows are staged in shared memory once per CTA instead of being loaded by every warp.
-// Staged vectors are stored half-major (vector 2k + h at h * V/2 + k), so the 32 lanes of a
-// warp read 32 consecutive 16-byte vectors (no bank conflicts).
+// of 16 per lane), so both row reductions are warp shuffles with no shared-memory round trip.
+// A CTA takes 8 * RPW rows (each warp RPW of them, one after another) and stages the norm
+// weight and the (at most two) modulation rows of its rows in shared memory once; the launch
+// uses this form only when the CTA's rows span at most two modulation rows
+// (rows_per_mod >= 8 * RPW - 1).  The first row's x is loaded before the staging barrier, so
+// its latency overlaps the staging.  Staged vectors are stored half-major (vector 2k + h at
+// h * V/2 + k), so the 32 lanes of a warp read 32 consecutive 16-byte vectors (no bank
+// conflicts).
+constexpr int kAdaRowsPerWarp = 2;
+
 template <int D, bool MUL, bool ADD>
 __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) {
   using G = RowQ<D, 1>;
   static_assert(G::W == 1 && G::R == 8, "one warp per row");
   constexpr int V = D / 8;  // 16-byte vectors per row
+  constexpr int RPW = kAdaRowsPerWarp;
   __shared__ __align__(16) uint4 s_w[V];
   __shared__ __align__(16) uint4 s_mod[2][2][(MUL || ADD) ? V : 1];  // [modulation row][scale1, shift]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t m_first = (int64_t)blockIdx.x * G::R;
-  const int64_t m = m_first + warp;
+  const int64_t m_first = (int64_t)blockIdx.x * G::R * RPW;
   const bool cta_live = m_first < a.M;
   const int64_t b0 = cta_live ? m_first / a.rows_per_mod : 0;
-  const int64_t b1 = cta_live ? min(m_first + G::R - 1, a.M - 1) / a.rows_per_mod : 0;
+  const int64_t b1 = cta_live ? min(m_first + G::R * RPW - 1, a.M - 1) / a.rows_per_mod : 0;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  uint4 xv[2 * G::NB];
+  auto load_row = [&](int64_t m) {
+    const bool pad = m >= a.M;
+    const uint4* row = reinterpret_cast<const uint4*>(a.x + (pad ? 0 : m) * a.ldx);
+#pragma unroll
+    for (int j = 0; j < G::NB; ++j) {
+      const int kb = j * 32 + lane;
+      xv[2 * j] = pad ? z : __ldg(row + 2 * kb);
+      xv[2 * j + 1] = pad ? z : __ldg(row + 2 * kb + 1);
+    }
+  };
+  load_row(m_first + warp);  // in flight across the staging below
   if (cta_live) {
     const uint4* wsrc = reinterpret_cast<const uint4*>(a.norm_w);
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -181,59 +199,55 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
     }
   }
   __syncthreads();
-  const bool pad = m >= a.M;
-  const uint4* row = reinterpret_cast<const uint4*>(a.x + (pad ? 0 : m) * a.ldx);
-  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  uint4 xv[2 * G::NB];
+#pragma unroll 1
+  for (int rw = 0; rw < RPW; ++rw) {
+    const int64_t m = m_first + rw * G::R + warp;
+    if (rw > 0) load_row(m);
+    const bool pad = m >= a.M;
+    float ss = 0.0f;
 #pragma unroll
-  for (int j = 0; j < G::NB; ++j) {
-    const int kb = j * 32 + lane;
-    xv[2 * j] = pad ? z : __ldg(row + 2 * kb);
-    xv[2 * j + 1] = pad ? z : __ldg(row + 2 * kb + 1);
-  }
-  float ss = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
-  ss = warp_sum(ss);
-  const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
-  const int sel = (!pad && (MUL || ADD) && m / a.rows_per_mod != b0) ? 1 : 0;
-  float am = 0.0f;
-#pragma unroll
-  for (int j = 0; j < G::NB; ++j) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = h * (V / 2) + j * 32 + lane;  // vector 2 (j * 32 + lane) + h, half-major
-      const uint4 sv = MUL ? s_mod[sel][0][c] : z, hv = ADD ? s_mod[sel][1][c] : z;
-      xv[2 * j + h] = norm8<MUL, ADD>(xv[2 * j + h], s_w[c], sv, hv, rinv);
-      am = fmaxf(am, absmax8_fast(xv[2 * j + h]));
-    }
-  }
-  if (a.y && !pad) {
-    uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
+    for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
+    ss = warp_sum(ss);
+    const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
+    const int sel = (!pad && (MUL || ADD) && m / a.rows_per_mod != b0) ? 1 : 0;
+    float am = 0.0f;
 #pragma unroll
     for (int j = 0; j < G::NB; ++j) {
-      const int kb = j * 32 + lane;
-      yrow[2 * kb] = xv[2 * j];
-      yrow[2 * kb + 1] = xv[2 * j + 1];
-    }
-  }
-  if (!a.codes) return;
-  am = warp_max(am);
-  if (m >= a.Mpad) return;
-  const int64_t r = m & 127;
-  uint8_t* sf_rowbase = a.sf + (m >> 7) * (D / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
-  if (pad) {  // padding rows of the scale layout: zero scales
-    for (int c = lane; c < D / 64; c += 32) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
-    return;
-  }
-  const float g = global_scale(am);
-  if (lane == 0) a.gs[m] = g;
-  const float denom = __fmul_rn(6.0f, g);
-  uint8_t* code_row = a.codes + m * (D / 2);
 #pragma unroll
-  for (int j = 0; j < G::NB; ++j) {
-    const int64_t kb = (int64_t)j * 32 + lane;
-    store_block(quant_block(xv[2 * j], xv[2 * j + 1], g, denom), true, kb, lane, code_row, sf_rowbase);
+      for (int h = 0; h < 2; ++h) {
+        const int c = h * (V / 2) + j * 32 + lane;  // vector 2 (j * 32 + lane) + h, half-major
+        const uint4 sv = MUL ? s_mod[sel][0][c] : z, hv = ADD ? s_mod[sel][1][c] : z;
+        xv[2 * j + h] = norm8<MUL, ADD>(xv[2 * j + h], s_w[c], sv, hv, rinv);
+        am = fmaxf(am, absmax8_fast(xv[2 * j + h]));
+      }
+    }
+    if (a.y && !pad) {
+      uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
+#pragma unroll
+      for (int j = 0; j < G::NB; ++j) {
+        const int kb = j * 32 + lane;
+        yrow[2 * kb] = xv[2 * j];
+        yrow[2 * kb + 1] = xv[2 * j + 1];
+      }
+    }
+    if (!a.codes) continue;
+    am = warp_max(am);
+    if (m >= a.Mpad) continue;
+    const int64_t r = m & 127;
+    uint8_t* sf_rowbase = a.sf + (m >> 7) * (D / 64) * 512 + (r & 31) * 16 + (r >> 5) * 4;
+    if (pad) {  // padding rows of the scale layout: zero scales
+      for (int c = lane; c < D / 64; c += 32) *reinterpret_cast<uint32_t*>(sf_rowbase + c * 512) = 0u;
+      continue;
+    }
+    const float g = global_scale(am);
+    if (lane == 0) a.gs[m] = g;
+    const float denom = __fmul_rn(6.0f, g);
+    uint8_t* code_row = a.codes + m * (D / 2);
+#pragma unroll
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t kb = (int64_t)j * 32 + lane;
+      store_block(quant_block(xv[2 * j], xv[2 * j + 1], g, denom), true, kb, lane, code_row, sf_rowbase);
+    }
   }
 }
 
@@ -366,12 +380,15 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const HeadArgs a) {
 template <int D>
 void launch_adanorm_d(const NormArgs& a, cudaStream_t st) {
   if constexpr (D == 2048) {
-    const dim3 grid((unsigned)((a.Mpad + 7) / 8));
-    if (a.scale1 && a.shift) adanorm_warp_kernel<D, true, true><<<grid, 256, 0, st>>>(a);
-    else if (a.scale1) adanorm_warp_kernel<D, true, false><<<grid, 256, 0, st>>>(a);
-    else if (a.shift) adanorm_warp_kernel<D, false, true><<<grid, 256, 0, st>>>(a);
-    else adanorm_warp_kernel<D, false, false><<<grid, 256, 0, st>>>(a);
-    return;
+    // the staged form needs the CTA's rows to span at most two modulation rows
+    if ((!a.scale1 && !a.shift) || a.rows_per_mod >= 8 * kAdaRowsPerWarp - 1) {
+      const dim3 grid((unsigned)((a.Mpad + 8 * kAdaRowsPerWarp - 1) / (8 * kAdaRowsPerWarp)));
+      if (a.scale1 && a.shift) adanorm_warp_kernel<D, true, true><<<grid, 256, 0, st>>>(a);
+      else if (a.scale1) adanorm_warp_kernel<D, true, false><<<grid, 256, 0, st>>>(a);
+      else if (a.shift) adanorm_warp_kernel<D, false, true><<<grid, 256, 0, st>>>(a);
+      else adanorm_warp_kernel<D, false, false><<<grid, 256, 0, st>>>(a);
+      return;
+    }
   }
   const dim3 grid((unsigned)((a.Mpad + RowQ<D>::R - 1) / RowQ<D>::R));
   if (a.scale1 && a.shift) adanorm_quant_kernel<D, true, true><<<grid, 256, 0, st>>>(a);

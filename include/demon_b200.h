@@ -305,6 +305,13 @@ DEMON_API int demon_ode_step(const DemonOdeSlot* slots_dev, int32_t n_slots, int
 DEMON_API int demon_ode_prepare(const DemonOdeSlot* slots_dev, int32_t n_slots, int64_t T, int64_t D, const void* gain,
                       void* stream);
 
+/*
+ * CTAs per slot cluster that demon_ode_step / demon_ode_prepare launch for n_slots slots of
+ * T frames on the current device: 8 while all clusters of 8 are resident at once, else 4.
+ * Launches nothing (for tests and tuning).
+ */
+DEMON_API int demon_ode_cluster_size(int32_t n_slots, int64_t T, int32_t* cluster);
+
 #ifdef __cplusplus
 }
 #endif

@@ -151,12 +151,24 @@ def check(name, got, ref, scale):
     assert exact >= 0.99, (name, exact)
 
 
-@pytest.mark.parametrize("T,n", [(750, None), (123, None), (1500, None), (301, 64)])
+def _slots_for_cluster(T, cl):
+    """The fewest slots for which the ODE launch takes `cl`-CTA clusters on this device."""
+    from demon_b200 import _native
+    for n in range(1, 4096):
+        if _native.ode_cluster_size(n, T) == cl:
+            return n
+    pytest.skip(f"no slot count takes {cl}-CTA clusters here")
+
+
+@pytest.mark.parametrize("T,n", [(750, None), (123, None), (1500, None), (301, 64), (301, "cl4"), (301, "cl8"),
+                                 (301, "cl9"), (301, "cl12"), (301, "cl16")])
 def test_ode_step_matches_oracle(cuda, T, n):
-    """Every kind of slot once (n None), or n slots cycling through the kinds: 64 slots on a
-    148-SM B200 take the launch form with 4-CTA clusters (8-CTA clusters would need a second
-    wave of CTAs), fewer take 8-CTA clusters."""
+    """Every kind of slot once (n None), or n slots cycling through the kinds.  The launch's
+    cluster size (CTAs per slot: 4, 8, 9, 12 or 16) follows the slot count; "clX" takes the
+    fewest slots for which the launch uses X (skipped when no slot count does on this GPU)."""
     from demon_b200 import ode
+    if isinstance(n, str):
+        n = _slots_for_cluster(T, int(n[2:]))
     rng = np.random.default_rng(T)
     kinds = KINDS if n is None else [KINDS[i % len(KINDS)] for i in range(n)]
     specs = [make_spec(rng, T, k) for k in kinds]
