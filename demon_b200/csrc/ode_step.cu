@@ -112,7 +112,11 @@ struct OdeShared {
 // fp32 operation followed by rounding to bf16; an fp32 scalar times a bf16 tensor goes
 // through fp32 (mul_f2) and is rounded afterwards (f2_bf2), as torch's opmath does.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t sub_bf2(uint32_t a, uint32_t b) { return add_bf2(a, b ^ 0x80008000u); }
+__device__ __forceinline__ uint32_t sub_bf2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 __device__ __forceinline__ uint32_t bf2_dup(float v) { return pack_bf16x2(v, v); }  // v already bf16-exact
 __device__ __forceinline__ float2 f2_dup(float v) { return make_float2(v, v); }
 // bf16(s * x) for an fp32 scalar s and a bf16 pair x
@@ -636,10 +640,6 @@ static cudaLaunchConfig_t ode_launch_cfg(int n, int64_t T, int cl, cudaStream_t 
   return cfg;
 }
 
-// Cluster sizes the launch chooses from (CTAs per slot); above 8 they are non-portable sizes.
-constexpr int kOdeClusterSizes[] = {4, 8, 9, 12, 16};
-constexpr int kOdeNumCl = 5;
-
 template <int CL>
 static int ode_prepare_kernel_attrs() {
   const int dyn_max = 227 * 1024 - (int)sizeof(OdeShared) - (int)sizeof(DemonOdeSlot) - 1024;
@@ -656,57 +656,44 @@ static int ode_resident_clusters(int64_t T, int* out) {
   return DEMON_OK;
 }
 
-// CTAs per slot cluster for n slots of T frames on the current device.  Every slot's cluster
-// should be resident at once (one wave), and the busiest SM should hold as few rows as possible:
-// among the sizes whose n clusters fit (resident-cluster counts from the occupancy calculator),
-// the one with the least ceil(n * CL / SMs) * rows-per-CTA, the larger size on a tie (more
-// warps per SM to hide latency: 64 slots x T=1500 run 45.5 us in 8-CTA clusters, 55.9 us in
-// 4-CTA clusters of the same cost); 4 when none fits.  8 slots take 16 (128 CTAs of 94 rows)
-// rather than 8 (64 CTAs on 64 SMs).  The counts are cached per device for the last T (T sets
-// the row table's size).
+// CTAs per slot cluster for n slots of T frames on the current device: 16 (a non-portable size)
+// while the n * 16 CTAs need no more than one per SM, else 8 while all n clusters of 8 are
+// resident at once, else 4 (half the CTAs, twice the rows each).  Resident-cluster counts come
+// from the occupancy calculator, cached per device for the last T (T sets the row table's
+// size).  Measured at T=1500: 8 slots 16.1 us in 16-CTA clusters against 19.1 in 8-CTA ones;
+// 64 slots 45.9 us in 8-CTA clusters against 55.9 in 4-CTA ones.  Odd sizes between (9 or 12
+// CTAs, fewer rows on the busiest SM on paper) measured no faster at 16 slots and slower at 32
+// (34.0 us against 28.6), the hardware packing clusters into GPCs unevenly.
 static int ode_cluster(int n, int64_t T, int* cl) {
   static std::atomic<uint64_t> attr_done{0};
   static int sms = 0;
   if (device_pending(attr_done)) {
     if (int rc = ode_prepare_kernel_attrs<4>()) return rc;
     if (int rc = ode_prepare_kernel_attrs<8>()) return rc;
-    if (int rc = ode_prepare_kernel_attrs<9>()) return rc;
-    if (int rc = ode_prepare_kernel_attrs<12>()) return rc;
     if (int rc = ode_prepare_kernel_attrs<16>()) return rc;
     int dev = 0;
     DEMON_CUDA(cudaGetDevice(&dev));
     DEMON_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     mark_device_done(attr_done);
   }
-  // per device: T in the top 16 bits, then one 9-bit resident-cluster count per size
+  // per device: T in the top 32 bits, then the resident 16- and 8-CTA cluster counts
   static std::atomic<uint64_t> occ_cache[64];
   int dev = 0;
   DEMON_CUDA(cudaGetDevice(&dev));
   const uint64_t cached = dev < 64 ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
-  int mc[kOdeNumCl];
-  if (cached != 0 && (int64_t)(cached >> 48) == T) {
-    for (int i = 0; i < kOdeNumCl; ++i) mc[i] = (int)((cached >> (9 * i)) & 511u);
+  int mc16 = 0, mc8 = 0;
+  if (cached != 0 && (int64_t)(cached >> 32) == T) {
+    mc16 = (int)((cached >> 16) & 0xFFFF);
+    mc8 = (int)(cached & 0xFFFF);
   } else {
-    if (int rc = ode_resident_clusters<4>(T, &mc[0])) return rc;
-    if (int rc = ode_resident_clusters<8>(T, &mc[1])) return rc;
-    if (int rc = ode_resident_clusters<9>(T, &mc[2])) return rc;
-    if (int rc = ode_resident_clusters<12>(T, &mc[3])) return rc;
-    if (int rc = ode_resident_clusters<16>(T, &mc[4])) return rc;
-    uint64_t word = (uint64_t)T << 48;
-    for (int i = 0; i < kOdeNumCl; ++i) word |= (uint64_t)std::min(std::max(mc[i], 0), 511) << (9 * i);
-    if (dev < 64) occ_cache[dev].store(word, std::memory_order_relaxed);
+    if (int rc = ode_resident_clusters<16>(T, &mc16)) return rc;
+    if (int rc = ode_resident_clusters<8>(T, &mc8)) return rc;
+    mc16 = std::min(std::max(mc16, 0), 0xFFFF);
+    mc8 = std::min(std::max(mc8, 0), 0xFFFF);
+    if (dev < 64) occ_cache[dev].store(((uint64_t)T << 32) | ((uint64_t)mc16 << 16) | (uint64_t)mc8, std::memory_order_relaxed);
   }
   const int64_t nsm = sms > 0 ? sms : 148;
-  int best = 4;
-  int64_t best_cost = -1;
-  for (int i = 0; i < kOdeNumCl; ++i) {
-    const int c = kOdeClusterSizes[i];
-    if (n > mc[i]) continue;
-    const int64_t per_sm = ((int64_t)n * c + nsm - 1) / nsm;
-    const int64_t cost = per_sm * ode_rows_per_cta((int)T, c);
-    if (best_cost < 0 || cost <= best_cost) best = c, best_cost = cost;  // ties: more, smaller CTAs
-  }
-  *cl = best;
+  *cl = ((int64_t)n * 16 <= nsm && n <= mc16) ? 16 : n <= mc8 ? 8 : 4;
   return DEMON_OK;
 }
 
@@ -732,8 +719,6 @@ int launch_ode(const DemonOdeSlot* slots, int32_t n, int64_t T, int64_t D, const
   const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(gain);
   switch (cl) {
     case 16: DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<16>, slots, (int)T, g, prepare_only)); break;
-    case 12: DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<12>, slots, (int)T, g, prepare_only)); break;
-    case 9: DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<9>, slots, (int)T, g, prepare_only)); break;
     case 8: DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<8>, slots, (int)T, g, prepare_only)); break;
     default: DEMON_CUDA(cudaLaunchKernelEx(&cfg, ode_step_kernel<4>, slots, (int)T, g, prepare_only)); break;
   }

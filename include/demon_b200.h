@@ -307,8 +307,8 @@ DEMON_API int demon_ode_prepare(const DemonOdeSlot* slots_dev, int32_t n_slots, 
 
 /*
  * CTAs per slot cluster that demon_ode_step / demon_ode_prepare launch for n_slots slots of
- * T frames on the current device: 8 while all clusters of 8 are resident at once, else 4.
- * Launches nothing (for tests and tuning).
+ * T frames on the current device: 16 while the CTAs need at most one per SM, else 8 while all
+ * clusters of 8 are resident at once, else 4.  Launches nothing (for tests and tuning).
  */
 DEMON_API int demon_ode_cluster_size(int32_t n_slots, int64_t T, int32_t* cluster);
 

@@ -51,8 +51,11 @@ def oracle_quant_of(y_bf16_cpu):
     return O.quantize(bits, O.GS_PER_ROW)
 
 
-@pytest.mark.parametrize("M,D,B", [(300, 2048, 2), (77, 256, 1), (130, 6144, 5)])
+@pytest.mark.parametrize("M,D,B", [(300, 2048, 2), (300, 2048, 20), (300, 2048, 100), (77, 256, 1), (130, 6144, 5)])
 def test_adanorm_quantize(cuda, M, D, B):
+    """B modulation rows over M rows (S = ceil(M / B) rows each).  At D = 2048 a CTA of the
+    staged kernel covers 16 rows and stages two modulation rows: S = 15 (B = 20) is the smallest
+    S it takes, S = 3 (B = 100) goes to the per-warp form."""
     from demon_b200.rowops import adanorm_quantize
     S = -(-M // B)
     g = torch.Generator().manual_seed(M + D)
