@@ -974,6 +974,12 @@ def run_kernel_workload(args):
             out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             launches.append((f"gemm {M}x{N}x{K}", 2.0 * M * N * K,
                              lambda a=a, pw=pw, out=out: nvfp4.gemm(a, pw, out=out)))
+            if args.vs_cublaslt:  # the library's block-scaled NVFP4 GEMM on the same packed operands
+                fa, fb = a.codes.view(torch.float4_e2m1fn_x2), pw.codes.view(torch.float4_e2m1fn_x2).t()
+                sa, sb = a.sf.view(torch.float8_e4m3fn), pw.sf.view(torch.float8_e4m3fn)
+                launches.append((f"cublaslt {M}x{N}x{K}", 2.0 * M * N * K,
+                                 lambda fa=fa, fb=fb, sa=sa, sb=sb: torch._scaled_mm(
+                                     fa, fb, sa, sb, out_dtype=torch.bfloat16)))
     else:
         from demon_b200.rowops import adanorm_quantize, silu_mul_quantize
         tick, nbytes, gain = ode_workload(dev, nslots=64, T=1500, seed=0)
@@ -1018,6 +1024,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows"])
+    ap.add_argument("--vs-cublaslt", action="store_true",
+                    help="with --workload gemm: also time cuBLASLt's NVFP4 GEMM (torch._scaled_mm) on the same operands")
     ap.add_argument("--shape", default="12000,6144,2048", help="M,N,K[:M,N,K...] of --workload gemm")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-ode", dest="ode", action="store_false", help="skip the ODE-step roofline leg")

@@ -174,6 +174,30 @@ def test_lora_path_alone(cuda):
     assert rel_fro(y, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(1500, 6144, 2048), (300, 2048, 6144), (129, 384, 256)])
+def test_gemm_matches_cublaslt_nvfp4(cuda, M, N, K):
+    """An independent implementation on the same packed operands: cuBLASLt's block-scaled NVFP4
+    GEMM (through torch._scaled_mm; E2M1 codes, E4M3 scales in the same 128x4-chunk layout, no
+    global scales).  demon's output divided by its alpha = a_gs[m] * w_gs must agree to the bf16
+    rounding of the two outputs."""
+    from demon_b200 import nvfp4
+    if not hasattr(torch, "float4_e2m1fn_x2"):
+        pytest.skip("this torch has no NVFP4 dtype")
+    x = make_x(M, K, seed=M + N).to(cuda)
+    w = make_w(N, K, seed=K).to(cuda)
+    a, pw = nvfp4.quantize(x), nvfp4.pack_weight(w)
+    y = nvfp4.gemm(a, pw)
+    try:
+        ref = torch._scaled_mm(a.codes.view(torch.float4_e2m1fn_x2), pw.codes.view(torch.float4_e2m1fn_x2).t(),
+                               a.sf.view(torch.float8_e4m3fn), pw.sf.view(torch.float8_e4m3fn),
+                               out_dtype=torch.bfloat16)
+    except (RuntimeError, TypeError) as e:  # a torch / cuBLASLt build without the NVFP4 path
+        pytest.skip(f"cuBLASLt NVFP4 GEMM unavailable: {e}")
+    alpha = a.gs.view(-1, 1).float() * pw.gs.view(1, -1).float()
+    d = y.float() / alpha
+    assert rel_fro(d.cpu(), ref.float().cpu()) < 5e-3
+
+
 def test_gemm_rows_are_batch_invariant(cuda):
     """A row's output does not depend on the other rows of the batch (stream == batch)."""
     from demon_b200 import nvfp4
