@@ -318,8 +318,9 @@ def measure_quantize(sets, stream, reps=8):
 
 
 def measure_quantize_big(dev, stream, M=12000, K=2048, reps=10):
-    """Quantiser HBM roofline at the tick's activation size (x bf16 [12000, 2048]: one o_proj
-    input of the 8-GPU ring, 49 MB), alternating two inputs (98 MB) so L2 holds neither."""
+    """Quantiser HBM roofline at a tick's activation size (x bf16 [M, 2048], the rank's rows of
+    one forward: 2 x slots x 750 tokens), three inputs rotated so L2 holds none of them from one
+    launch to the next (at M = 12000, the 8-GPU ring's rank, 3 x 49 MB)."""
     import torch
     from demon_b200 import nvfp4
     xs = [torch.randn(M, K, device=dev).to(torch.bfloat16) for _ in range(3)]
@@ -874,7 +875,7 @@ def run_stream(args):
     groof_max = max_over_ranks(groof["ms"], dist_mod, dev)
     if rank == 0:
         pk = peaks()
-        quant = measure_quantize_big(dev, stream)
+        quant = measure_quantize_big(dev, stream, M=2 * r.local * (T5 // 2))
         odek = measure_ode(dev, stream) if args.ode else None
         lin = linear_leg(dev, stream)
         cfg3 = run_config3(dit, dev) if world == 1 else None
