@@ -14,7 +14,7 @@
 //
 // APG and cfg_rescale reduce over T for each (slot, channel) (dims=(1,), the
 // reference's default, ode_steps.py:328-336 and :365-370).  The T axis of a
-// slot is split over a 4- or 8-CTA thread-block cluster.  A first pass over a CTA's
+// slot is split over a 4-, 8- or 16-CTA thread-block cluster.  A first pass over a CTA's
 // rows streams v_pos, v_neg and the old momentum, stores the new momentum and
 // accumulates per-channel moments in registers; the cluster exchanges the
 // partial moments through distributed shared memory; the second pass streams
