@@ -242,3 +242,41 @@ def test_ode_in_kernel_noise_is_deterministic_and_gaussian(cuda):
     assert torch.equal(outs[0], outs[1])
     z = outs[0] / 0.5  # bare SDE: xt = t_next * noise + (1 - t_next) * 0
     assert abs(float(z.mean())) < 0.02 and abs(float(z.std()) - 1.0) < 0.02
+
+
+def test_ode_rejects_bad_launches(cuda):
+    """Shape and alignment checks run on the host before any launch: each bad argument raises
+    DemonError through the C ABI, and the device status stays clean."""
+    from demon_b200 import _native
+    L = _native.load()
+    table = torch.zeros(4096, dtype=torch.uint8, device=cuda)  # never read: every call is rejected
+    gain = torch.zeros(2 * 64 + 8, dtype=torch.bfloat16, device=cuda)
+    sp = _native.stream_ptr()
+    bad = [
+        (table.data_ptr(), 0, 100, 64, 0),                       # no slots
+        (table.data_ptr(), 1, 0, 64, 0),                         # T = 0
+        (table.data_ptr(), 1, 6401, 64, 0),                      # T above the maximum
+        (table.data_ptr(), 1, 100, 32, 0),                       # latent width other than 64
+        (table.data_ptr(), 4096, 100, 64, 0),                    # more slots than the grid allows
+        (table.data_ptr() + 4, 1, 100, 64, 0),                   # slot table not 8-byte aligned
+        (table.data_ptr(), 1, 100, 64, gain.data_ptr() + 2),     # gain not 16-byte aligned
+    ]
+    for args in bad:
+        for fn in (L.demon_ode_step, L.demon_ode_prepare):
+            with pytest.raises(_native.DemonError):
+                _native.check(fn(*args, sp))
+    with pytest.raises(_native.DemonError):
+        _native.ode_cluster_size(1, 0)
+    assert _native.device_status() == (0, 0)
+
+
+def test_ode_cluster_size_choices(cuda):
+    """One slot spreads over 16 CTAs (one per SM); a full B200 ring of 64 slots at T=1500 takes
+    8-CTA clusters; far more slots than fit at once fall back to 4."""
+    from demon_b200 import _native
+    sizes = {n: _native.ode_cluster_size(n, 1500) for n in (1, 9, 10, 64, 400, 4095)}
+    assert set(sizes.values()) <= {4, 8, 16}
+    assert sizes[1] == 16 and sizes[4095] == 4
+    n_sm = torch.cuda.get_device_properties(cuda).multi_processor_count
+    if n_sm >= 148:
+        assert sizes[9] in (8, 16) and sizes[10] == 8 and sizes[64] == 8
