@@ -286,13 +286,16 @@ def prepare_dec(s: dict, rnd=bf16):
     return x
 
 
-def schedule(steps: int, shift: float, denoise: float, rnd=bf16) -> np.ndarray:
-    """DiffusionEngine._build_timestep_schedule (acestep/engine/diffusion.py:656-699),
-    evaluated in the pipeline dtype like the reference (stream.py:385-396)."""
+def schedule(steps: int, shift: float, denoise: float) -> np.ndarray:
+    """DiffusionEngine._build_timestep_schedule (acestep/engine/diffusion.py:656-699), evaluated
+    in bfloat16 like the reference (stream.py:385-396): torch's linspace in the pipeline dtype
+    (a numpy linspace rounded afterwards differs in the last bit for truncated schedules), then
+    the shift as bf16 tensor ops.  Pinned by tests/golden/schedule_golden.json."""
+    import torch
     if denoise <= 1e-6:
         return np.zeros(2)
     t_start = 1.0 if denoise >= 1.0 else steps / int(steps / denoise)
-    t = rnd(np.linspace(t_start, 0.0, steps + 1))
+    t = torch.linspace(t_start, 0.0, steps + 1, dtype=torch.bfloat16)
     if shift != 1.0:
-        t = rnd(rnd(shift * t) / rnd(1 + rnd(rnd(shift - 1) * t)))
-    return t
+        t = shift * t / (1 + (shift - 1) * t)
+    return t.float().numpy().astype(np.float64)
