@@ -361,9 +361,13 @@ class StreamPipeline:
                                                            self._dtype)
         return self._schedule_cache[denoise]
 
-    def _make_noise(self, req: SlotRequest, T: int, D: int) -> torch.Tensor:
-        """stream.py:403-451 (noise_on_cpu: CPU randn [1, D, T] per seed, then transposed)."""
-        seed = req.seed
+    @staticmethod
+    def noise_host(seed, T: int, D: int, dtype=torch.bfloat16) -> torch.Tensor:
+        """A slot's initial noise [T, D] on the host, as the reference draws it
+        (StreamPipeline._make_noise, stream.py:403-451, with noise_on_cpu, its default): torch's
+        CPU generator, randn [1, D, T] per seed (an int seeds once, a list seeds row by row and a
+        negative or None entry keeps the generator's state), transposed to [T, D] and rounded to
+        the pipeline dtype.  A slot holds one sample: with a list of seeds its first row."""
         if isinstance(seed, list):
             rows = []
             for s in seed:
@@ -375,7 +379,11 @@ class StreamPipeline:
             if seed is not None:
                 torch.manual_seed(int(seed))
             n = torch.randn(1, D, T, dtype=torch.float32)
-        host = n.movedim(-1, -2)[0].to(self._dtype).contiguous()   # bf16 rounding as .to(dtype) does
+        return n.movedim(-1, -2)[0].to(dtype).contiguous()   # bf16 rounding as .to(dtype) does
+
+    def _make_noise(self, req: SlotRequest, T: int, D: int) -> torch.Tensor:
+        """The initial noise (noise_host) uploaded to the device."""
+        host = self.noise_host(req.seed, T, D, self._dtype)
         # upload through a ring of pinned buffers (a pageable copy would stall the host on the GPU)
         k = self._stage_i = (self._stage_i + 1) % len(self._stage)
         buf, ev = self._stage[k]
