@@ -92,3 +92,56 @@ def test_sharded_ring_two_ranks():
     # tick's set handed over at the next step (the first step returns the empty set before it)
     assert res[1][2] == []
     assert res[0][2] == [[]] + [[100.0 * (t % 2) + t] for t in range(12)]
+
+
+def _failing_worker(rank, world, port, q, fail_at):
+    """Rank 1 dies on the host between two ticks (no collective in flight); rank 0 must learn of
+    it through its next collective, which ends with an error inside the short group timeout
+    instead of waiting for good."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import time
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from demon_b200.ring import ShardedRing
+    ring = ShardedRing(FakePipe(rank), rank, world, T, "cpu", curve_names=["velocity_scale"], curve_every=1,
+                       max_finished=2)
+
+    def src(tick):
+        return {"velocity_scale": torch.full((T,), 1.0 + tick)}
+    for i in range(8):
+        if rank == 1 and i == fail_at:
+            _report(q, (rank, "left", i))
+            os._exit(3)  # the failure: the process leaves without joining the next collective
+        t0 = time.monotonic()
+        try:
+            ring.step(src)
+        except Exception as e:  # noqa: BLE001 -- any collective error is the detection
+            _report(q, (rank, f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}", i))
+            os._exit(0)
+    _report(q, (rank, "finished", 8))
+    os._exit(0)
+
+
+def _report(q, msg):
+    q.put(msg)
+    q.close()
+    q.join_thread()  # flush before the process exits without cleanup
+
+
+def test_sharded_ring_rank_failure_is_detected():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q, 3)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, what, i = q.get(timeout=120)
+        res[r] = (what, i)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == ("left", 3)
+    assert res[0][0].startswith("error"), res[0]
+    assert res[0][1] == 3  # the first tick after the peer left
+    assert procs[1].exitcode == 3
