@@ -9,6 +9,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "../../include/demon_b200.h"
+
 namespace demon {
 
 void set_error(const char* fmt, ...);
@@ -25,6 +27,13 @@ void mark_device_done(std::atomic<uint64_t>& flags);
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
                  uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+
+// Host-only argument checks of demon_nvfp4_quantize / demon_nvfp4_gemm (no CUDA call, no
+// launch): DEMON_OK, or DEMON_ERR_INVALID with the message set.  The entry points run them
+// first; callers that chain both kernels run both before launching either.
+int quantize_check(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, const float* gs,
+                   const uint8_t* codes, const uint8_t* sf);
+int gemm_check(const DemonGemmArgs* a);
 
 }  // namespace demon
 

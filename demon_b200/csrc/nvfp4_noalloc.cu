@@ -11,14 +11,20 @@
 // (x and the packed weight) and the output.
 //
 // Limits and behaviour:
-//   - the array is 4.875 MiB (demon_nvfp4_noalloc_scratch_bytes()) and exists on every GPU
-//     that loads the library, until the process exits;
+//   - the array is 4.875 MiB (demon_nvfp4_noalloc_scratch_bytes()).  It belongs to this
+//     library's device code: with CUDA's default lazy module loading it is set up in a
+//     device's context when the library's module is first loaded there (at the latest on
+//     the first call of this entry point on that device) and stays until the context ends;
 //   - it holds at most M * K <= 8,388,608 activation elements (4 MiB of codes),
 //     block scales of up to 640 KiB and per-row scales for up to 65,536 rows;
 //     larger calls are rejected with DEMON_ERR_INVALID before anything runs;
+//   - every argument check of both kernels (shape, strides, alignment, null pointers)
+//     runs on the host before the first launch, so a rejected call launches nothing and
+//     leaves the array untouched;
 //   - the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (once per device, with that device current); make
-//     that first call before any stream capture;
+//     cudaGetSymbolAddress (once per device, with that device current); that lookup can
+//     also be where the module gets loaded, so make the first call before any stream
+//     capture;
 //   - every call on a device shares the array and leaves the last call's
 //     contents in it.  Nothing in it has to start at zero: the per-row
 //     quantiser rewrites every code, block scale (padding rows included) and
@@ -82,16 +88,12 @@ extern "C" int demon_nvfp4_linear_noalloc(const void* x, int64_t M, int64_t K, i
                   "noalloc: block scales need %lld bytes, the scratch holds %lld", (long long)demon_nvfp4_sf_bytes(M, K),
                   (long long)kSfBytes);
   DEMON_CHECK_ARG(M <= kGsRows, "noalloc: M=%lld exceeds the %lld-row limit", (long long)M, (long long)kGsRows);
-  if (M == 0) return DEMON_OK;
   uint8_t* base = nullptr;
   const int rc0 = scratch_ptr(&base);
   if (rc0 != DEMON_OK) return rc0;
   uint8_t* codes = base;
   uint8_t* sf = base + kCodesBytes;
   float* gs = reinterpret_cast<float*>(base + kCodesBytes + kSfBytes);
-
-  int rc = demon_nvfp4_quantize(x, M, K, ldx, DEMON_GS_PER_ROW, gs, codes, sf, stream);
-  if (rc != DEMON_OK) return rc;
   DemonGemmArgs g;
   memset(&g, 0, sizeof g);
   g.a_codes = codes;
@@ -107,5 +109,13 @@ extern "C" int demon_nvfp4_linear_noalloc(const void* x, int64_t M, int64_t K, i
   g.out = out;
   g.ldo = ldo;
   g.bias = bias;
+  // both kernels' argument checks before either launches: a rejected call leaves the array alone
+  int rc = demon::quantize_check(x, M, K, ldx, DEMON_GS_PER_ROW, gs, codes, sf);
+  if (rc != DEMON_OK) return rc;
+  rc = demon::gemm_check(&g);
+  if (rc != DEMON_OK) return rc;
+  if (M == 0) return DEMON_OK;
+  rc = demon_nvfp4_quantize(x, M, K, ldx, DEMON_GS_PER_ROW, gs, codes, sf, stream);
+  if (rc != DEMON_OK) return rc;
   return demon_nvfp4_gemm(&g, stream);
 }

@@ -191,9 +191,9 @@ extern "C" int64_t demon_nvfp4_sf_bytes(int64_t rows, int64_t K) {
   return ((rows + 127) / 128) * 128 * (K / 16);
 }
 
-extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, float* gs,
-                                    uint8_t* codes, uint8_t* sf, void* stream) {
-  DEMON_API_BEGIN();
+namespace demon {
+int quantize_check(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, const float* gs,
+                   const uint8_t* codes, const uint8_t* sf) {
   DEMON_CHECK_ARG(M >= 0 && K > 0 && K % 64 == 0, "quantize: need K > 0, K %% 64 == 0 (K=%lld)", (long long)K);
   DEMON_CHECK_ARG(ldx >= K && ldx % 8 == 0, "quantize: ldx must be >= K and a multiple of 8 (ldx=%lld)",
                   (long long)ldx);
@@ -201,6 +201,15 @@ extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t
   DEMON_CHECK_ARG(gs != nullptr && (M == 0 || (x && codes && sf)), "quantize: null pointer");
   DEMON_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 3) == 0 && ((uintptr_t)sf & 3) == 0,
                   "quantize: x must be 16-byte aligned, codes/sf 4-byte aligned");
+  return DEMON_OK;
+}
+}  // namespace demon
+
+extern "C" int demon_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, int gs_mode, float* gs,
+                                    uint8_t* codes, uint8_t* sf, void* stream) {
+  DEMON_API_BEGIN();
+  const int rc0 = demon::quantize_check(x, M, K, ldx, gs_mode, gs, codes, sf);
+  if (rc0 != DEMON_OK) return rc0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t Mpad = (M + 127) / 128 * 128;
   if (Mpad == 0) return DEMON_OK;
