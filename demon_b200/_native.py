@@ -40,7 +40,7 @@ EXPORTED = (
     "demon_abi_version", "demon_struct_sizes", "demon_last_error", "demon_device_status",
     "demon_nvfp4_sf_bytes", "demon_nvfp4_quantize", "demon_nvfp4_gemm", "demon_lora_down",
     "demon_ode_step", "demon_ode_prepare", "demon_ode_cluster_size", "demon_nvfp4_noalloc_scratch_bytes",
-    "demon_nvfp4_linear_noalloc",
+    "demon_nvfp4_linear_noalloc", "demon_test_arm_gemm_stall",
     "demon_bf16_linear", "demon_adanorm_quantize", "demon_silu_mul_quantize", "demon_head_norm_rope",
 )
 
@@ -119,6 +119,7 @@ def load() -> ctypes.CDLL:
         L.demon_nvfp4_sf_bytes.argtypes = [_i64, _i64]
         L.demon_nvfp4_quantize.argtypes = [_vp, _i64, _i64, _i64, ctypes.c_int, _vp, _vp, _vp, _vp]
         L.demon_nvfp4_gemm.argtypes = [ctypes.POINTER(DemonGemmArgs), _vp]
+        L.demon_test_arm_gemm_stall.argtypes = [_i64]
         L.demon_lora_down.argtypes = [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, ctypes.c_int, _vp, _vp, _vp]
         L.demon_ode_step.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]
         L.demon_ode_prepare.argtypes = [_vp, _i32, _i64, _i64, _vp, _vp]

@@ -90,15 +90,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the completion of the phase with parity `parity`.
-// Returns false (and raises *abort) on timeout or if *abort is already set.
+// Returns false (and raises *abort) on timeout (`limit_ns` of device time since t0) or if
+// *abort is already set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t t0,
-                                          unsigned int* status, unsigned int where) {
+                                          unsigned int* status, unsigned int where,
+                                          uint64_t limit_ns = DEMON_WAIT_LIMIT_NS) {
   const uint32_t a = smem_u32(bar);
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 255u) == 255u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > DEMON_WAIT_LIMIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         report(status, DEMON_DEV_TIMEOUT, where);
         return false;

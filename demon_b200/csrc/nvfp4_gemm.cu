@@ -69,6 +69,10 @@ struct GemmParams {
   int m_tiles, n_tiles;
   int m_group;  // tile order: bands of m_group m-blocks, each swept over every n-block
   int silu_mul;  // SwiGLU epilogue: interleaved gate/up blocks of 128 -> h of width N / 2
+  // bounded-wait test (demon_test_arm_gemm_stall): the first CTA (pair) waits at most wait_ns
+  // and its rank-0 CTA withholds the loads of its first stage; 0 in normal launches
+  int withhold;
+  uint64_t wait_ns;
 };
 
 constexpr int kBM = 128;
@@ -163,6 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cid = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int ncl = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr int kTileM = PAIR ? 2 * kBM : kBM;
+  // wait limit of this CTA: the default, or the armed test's short one in the first CTA (pair)
+  const uint64_t lim = (p.withhold && cid == 0) ? p.wait_ns : (uint64_t)DEMON_WAIT_LIMIT_NS;
+  const bool hold0 = p.withhold && cid == 0 && rank == 0;  // test: skip the loads of stage 0
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -220,8 +227,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t mult = PAIR ? 2u : 1u;
         for (int b = 0; b < lboxes; ++b, ++g) {
           const int s = g % STAGES;
-          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 1))) break;
+          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 1, lim))) break;
           if (leader) mbar_arrive_expect_tx(&full[s], mult * (uint32_t)(C::kA + C::kB));
+          if (hold0 && g == 0) continue;  // test: these bytes never arrive
           if (PAIR) {
             tma_load_2d_pair(smem + C::offA + s * C::kA, &tmLA, &full[s], b * 64, am0);
             tma_load_2d_pair(smem + C::offB + s * C::kB, &tmLB, &full[s], b * 64, bn0);
@@ -235,8 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tx = (uint32_t)(C::kA + C::kB + C::kSFA + sfb_halves * 2048);
         for (int kt = 0; ok && kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
-          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 2))) break;
+          if (!(ok = mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, t0, p.status, 2, lim))) break;
           if (leader) mbar_arrive_expect_tx(&full[s], mult * tx);
+          if (hold0 && g == 0) continue;  // test: these bytes never arrive
           const int kx = FP4 ? kt * kRowBytes : kt * 64;
           if (PAIR) {
             tma_load_2d_pair(smem + C::offA + s * C::kA, &tmA, &full[s], kx, am0);
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!leader) g = 0;
       for (uint32_t i = g > (uint32_t)STAGES ? g - STAGES : 0; i < g; ++i) {
         volatile int never = 0;
-        mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never, globaltimer(), p.status, 3);
+        mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, &never, globaltimer(), p.status, 3, lim);
       }
     }
     __syncwarp();
@@ -280,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = cid; ok && tile < num_tiles; tile += ncl, ++it) {
         // the epilogue must have drained the previous tile's accumulator
-        if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4))) break;
+        if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4, lim))) break;
         tc_fence_after();
         uint32_t accum = 0;
         for (int b = 0; b < lboxes; ++b, ++g) {
           const int s = g % STAGES;
-          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 5))) break;
+          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 5, lim))) break;
           tc_fence_after();
           const uint64_t la = sw128_desc(smem + C::offA + s * C::kA);
           const uint64_t lb = sw128_desc(smem + C::offB + s * C::kB);
@@ -305,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int kt = 0; ok && kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
-          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 6))) break;
+          if (!(ok = mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, t0, p.status, 6, lim))) break;
           tc_fence_after();
           const uint64_t adesc = sw128_desc(smem + C::offA + s * C::kA);
           const uint64_t bdesc = sw128_desc(smem + C::offB + s * C::kB);
@@ -373,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) {  // both CTAs of a pair learn of the last MMA through their own barrier
       volatile int never = 0;
-      mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9);
+      mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9, lim);
     }
     __syncwarp();
   } else {
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (res_row) prefetch_l2(reinterpret_cast<const uint8_t*>(res_row) + j);
       }
       __syncwarp();
-      if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7)) break;
+      if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7, lim)) break;
       tc_fence_after();
       if (*abort_flag) break;
       uint32_t v[C::kChunks][32];
@@ -683,8 +692,8 @@ using namespace demon;
     if (_rc != DEMON_OK) return _rc; \
   } while (0)
 
-extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
-  DEMON_API_BEGIN();
+namespace demon {
+int gemm_check(const DemonGemmArgs* a) {
   DEMON_CHECK_ARG(a != nullptr, "gemm: null args");
   const int64_t M = a->M, N = a->N, K = a->K;
   DEMON_CHECK_ARG(M >= 0 && N > 0 && K > 0, "gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
@@ -694,6 +703,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   DEMON_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: dimension too large");
   DEMON_CHECK_ARG(a->a_codes && a->a_sf && a->a_gs && a->w_codes && a->w_sf && a->w_gs && a->out,
                   "gemm: null operand");
+  DEMON_CHECK_ARG(((uintptr_t)a->a_codes & 15) == 0 && ((uintptr_t)a->w_codes & 15) == 0,
+                  "gemm: code buffers must be 16-byte aligned");
   DEMON_CHECK_ARG(a->ldo >= (a->silu_mul ? N / 2 : N) && a->ldo % 8 == 0 && ((uintptr_t)a->out & 15) == 0,
                   "gemm: out needs ldo >= N (N / 2 with silu_mul), ldo %% 8 == 0, 16-byte alignment");
   DEMON_CHECK_ARG(!a->residual || (a->ldr >= N && a->ldr % 8 == 0 && ((uintptr_t)a->residual & 15) == 0),
@@ -708,6 +719,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   DEMON_CHECK_ARG(!lora || (a->lora_b && a->lora_rank > 0 && a->lora_rank % 16 == 0 && a->lora_rank <= 128),
                   "gemm: LoRA needs lora_b and rank %% 16 == 0, 0 < rank <= 128 (rank=%lld)",
                   (long long)a->lora_rank);
+  DEMON_CHECK_ARG(!lora || (((uintptr_t)a->lora_xa & 15) == 0 && ((uintptr_t)a->lora_b & 15) == 0),
+                  "gemm: LoRA operands must be 16-byte aligned");
   DEMON_CHECK_ARG(!(lora && a->w_gs_per_block), "gemm: hot LoRA needs a single weight scale (w_gs_per_block = 0)");
   if (a->hn_cols > 0) {
     DEMON_CHECK_ARG(N % 256 == 0 && a->hn_cols % 128 == 0 && a->hn_cols <= N && a->hn_q_cols >= 0 &&
@@ -723,8 +736,30 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   const bool silu = a->silu_mul != 0;
   DEMON_CHECK_ARG(!silu || (N % 256 == 0 && !lora && a->hn_cols == 0 && !a->gate && !a->residual),
                   "gemm: the SwiGLU epilogue needs N %% 256 == 0 and excludes LoRA, head norm, gate, residual");
+  return DEMON_OK;
+}
+
+namespace {
+// demon_test_arm_gemm_stall: wait limit (ns) for the next NVFP4 GEMM launch of this thread
+thread_local int64_t t_stall_wait_ns = 0;
+}  // namespace
+}  // namespace demon
+
+extern "C" int demon_test_arm_gemm_stall(int64_t wait_ns) {
+  DEMON_CHECK_ARG(wait_ns == 0 || (wait_ns >= 100000 && wait_ns <= 1000000000),
+                  "test_arm_gemm_stall: wait_ns must be 0 or in [1e5, 1e9] (%lld)", (long long)wait_ns);
+  demon::t_stall_wait_ns = wait_ns;
+  return DEMON_OK;
+}
+
+extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
+  DEMON_API_BEGIN();
+  const int rc0 = gemm_check(a);
+  if (rc0 != DEMON_OK) return rc0;
+  const int64_t M = a->M, N = a->N, K = a->K;
+  const bool lora = a->lora_xa != nullptr;
+  const bool silu = a->silu_mul != 0;
   const int64_t n_out = silu ? N / 2 : N;
-  DEMON_CHECK_ARG(!silu || a->ldo >= n_out, "gemm: SwiGLU output needs ldo >= N / 2");
   if (M == 0) return DEMON_OK;
 
   const bool bn256 = (N % 256 == 0);
@@ -787,6 +822,11 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   p.hn_eps = a->hn_eps;
   p.silu_mul = silu ? 1 : 0;
   p.lora_rank = lora ? (int)a->lora_rank : 0;
+  if (t_stall_wait_ns > 0) {  // armed bounded-wait test: one launch only
+    p.withhold = 1;
+    p.wait_ns = (uint64_t)t_stall_wait_ns;
+    t_stall_wait_ns = 0;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);

@@ -5,7 +5,11 @@
  * Conventions shared by every entry point:
  *   - all pointers are device pointers unless the name says host;
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
- *   - the library never allocates device memory; callers own every buffer;
+ *   - the library never allocates device memory at run time: callers own every
+ *     buffer, except two fixed file-scope device arrays that the library's device
+ *     code holds in each device context it is loaded into -- the 8-byte status word
+ *     and the demon_nvfp4_noalloc_scratch_bytes() bytes (4.875 MiB) of scratch that
+ *     demon_nvfp4_linear_noalloc uses;
  *   - return value 0 = DEMON_OK, otherwise a DEMON_ERR_* code, with a message
  *     retrievable through demon_last_error() (thread-local);
  *   - argument errors are detected on the host before any launch;
@@ -145,6 +149,18 @@ typedef struct DemonGemmArgs {
 DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);
 
 /*
+ * Test hook for the bounded device-side waits (no counterpart in the reference): arms the
+ * next demon_nvfp4_gemm launch made by the calling thread.  In that launch the first CTA
+ * (CTA pair) waits at most wait_ns of device time per wait, and its first CTA never issues
+ * the loads of its first pipeline stage, so the MMA issuer's wait on that stage runs out.
+ * The CTA then records DEMON_DEV_TIMEOUT in the status word (demon_device_status), stops
+ * issuing, waits (bounded) for the copies it issued, frees its tensor memory and returns;
+ * the other CTAs finish normally.  The output of the armed launch is undefined; later
+ * launches are unaffected.  wait_ns in [1e5, 1e9], or 0 to disarm.
+ */
+DEMON_API int demon_test_arm_gemm_stall(int64_t wait_ns);
+
+/*
  * LoRA down-projection for the fused epilogue (tcgen05 bf16 GEMM):
  *   xa[m, j] = col_scale[j] * sum_k x[m,k] * lora_a[j,k] / (a_gs[m|0] * w_gs[0])
  * x bf16 [M, ldx], lora_a bf16 [rank, K] (PEFT lora_A layout, acestep/engine/lora.py:294-302),
@@ -208,10 +224,14 @@ DEMON_API int demon_head_norm_rope(void* x, int64_t M, int64_t ld, int64_t col0,
  * reference: it is for callers that cannot allocate device memory while the
  * layer runs (a TensorRT plugin's enqueue(), a real-time thread that must not
  * block in cudaMalloc).  Limits: M * K <= 8,388,608, M <= 65,536, K % 256 == 0,
- * N % 128 == 0.  The array (demon_nvfp4_noalloc_scratch_bytes() bytes) lives on
- * every GPU that loads the library until exit and is shared by all calls on a
- * device: calls that overlap on the GPU race.  The first call on a device
- * looks up the array's address (make it before any stream capture).
+ * N % 128 == 0.  Every argument check of both kernels runs before the first
+ * launch, so a rejected call launches nothing.  The array
+ * (demon_nvfp4_noalloc_scratch_bytes() bytes) is set up in a device's context
+ * when the library's device code is first loaded there (at the latest on the
+ * first call on that device) and stays until the context ends; it is shared
+ * by all calls on a device: calls that overlap on the GPU race.  The first
+ * call on a device looks up the array's address, which may also load the
+ * module: make it before any stream capture.
  */
 DEMON_API int64_t demon_nvfp4_noalloc_scratch_bytes(void);
 DEMON_API int demon_nvfp4_linear_noalloc(const void* x, int64_t M, int64_t K, int64_t ldx, const uint8_t* w_codes,

@@ -48,6 +48,10 @@ def test_host_only_entry_points(lib):
     assert lib.demon_abi_version() == 1
     assert lib.demon_nvfp4_sf_bytes(1500, 2048) == 1536 * 128
     assert lib.demon_nvfp4_sf_bytes(1, 64) == 128 * 4
+    # the bounded-wait test hook validates its limit on the host (and 0 disarms it)
+    assert lib.demon_test_arm_gemm_stall(ctypes.c_int64(10)) == 1
+    assert lib.demon_test_arm_gemm_stall(ctypes.c_int64(5_000_000)) == 0
+    assert lib.demon_test_arm_gemm_stall(ctypes.c_int64(0)) == 0
 
 
 def test_compute_entry_points_fail_cleanly_without_gpu(lib):
