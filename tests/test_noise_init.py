@@ -1,4 +1,4 @@
-"""A slot's initial noise (SURVEY A14) against golden draws from the reference's own
+"""A slot's initial noise against golden draws from the reference's own
 StreamPipeline._make_noise (tests/golden/gen_noise_golden.py): int seeds and per-row seed
 lists (a negative entry keeps the generator's state), bit for bit in bfloat16."""
 import json

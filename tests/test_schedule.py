@@ -1,4 +1,4 @@
-"""Timestep schedule (SURVEY A13) against golden schedules from the reference's own
+"""Timestep schedule against golden schedules from the reference's own
 DiffusionEngine._build_timestep_schedule (tests/golden/gen_schedule_golden.py): the host's
 stream.build_schedule and the oracle's restatement, bit for bit in bfloat16."""
 import json
