@@ -331,10 +331,18 @@ class NVFP4Linear(torch.nn.Module):
 
         x: [..., K] bf16.  gate: [B, N] (one row per leading batch index, as the
         AdaLN gates of the DiT, turbo.py:525-546) or None.  residual: like the output.
-        a: ``quantize(x)`` when several linears share the input (q/k/v, gate/up).
+        The plain call goes through the registered op ``torch.ops.demon_b200.nvfp4_linear``;
+        a: ``quantize(x)`` when several linears share the input (q/k/v, gate/up) and
+        ``out`` (a preallocated output) take the direct path to the same kernels.
         """
         if self.packed is None:
             self.repack()
+        if a is None and out is None:
+            lo = self.lora.active()
+            A, B, cs = lo if lo is not None else (None, None, None)
+            p = self.packed
+            return torch.ops.demon_b200.nvfp4_linear(x, p.codes, p.sf, p.gs, self.bias, A, B, 1.0, residual, gate,
+                                                     cs)
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         if x2.stride(-1) != 1:
@@ -357,3 +365,65 @@ class NVFP4Linear(torch.nn.Module):
         y = gemm(a, self.packed, bias=self.bias, residual=res2, gate=gate2, gate_rows=gate_rows,
                  lora_xa=xa, lora_b=lb, out=out2)
         return y.reshape(*lead, self.out_features)
+
+
+# ---------------------------------------------------------------------------
+# torch.library op: the torch-op surface of the quantised linear
+# ---------------------------------------------------------------------------
+
+@torch.library.custom_op("demon_b200::nvfp4_linear", mutates_args=(), device_types="cuda")
+def nvfp4_linear(x: torch.Tensor, w_codes: torch.Tensor, w_sf: torch.Tensor, w_gs: torch.Tensor,
+                 bias: torch.Tensor | None = None, lora_A: torch.Tensor | None = None,
+                 lora_B: torch.Tensor | None = None, lora_scale: float = 1.0,
+                 residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                 lora_col_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + gate * (x W^T + bias + lora_scale * (x A^T) B^T)`` with W in NVFP4, as one op.
+
+    The drop-in for the DiT's ``nn.Linear`` call sites (acestep/models/
+    modeling_acestep_v15_turbo.py:286-289, 311-345, 377, 538) plus the gated residual after
+    o_proj / the MLP (turbo.py:525-546) and the hot LoRA delta ``W + s B @ A``
+    (acestep/engine/lora.py:316-319, 824-833) without rewriting W.
+
+    x bf16 [..., K]; w_codes uint8 [N, K/2], w_sf uint8 (tcgen05 scale layout), w_gs fp32 [1]
+    (or [N/128], one per 128-row block of a fused pack); bias bf16 [N]; lora_A bf16 [r, K] and
+    lora_B bf16 [N, r] (PEFT layout, r % 16 == 0, r <= 128); residual bf16 [..., N]; gate bf16
+    [B, N] with B dividing the rows of x (one gate row per sequence); lora_col_scale fp32 [r]
+    multiplies lora_scale per rank column (several LoRAs concatenated along the rank, each
+    with its strength, updated in place without re-capturing graphs).  CUDA only: there is no
+    CPU kernel.  Returns bf16 [..., N].
+    """
+    K = x.shape[-1]
+    N = w_codes.shape[0]
+    if w_codes.shape[1] * 2 != K:
+        raise ValueError(f"nvfp4_linear: w_codes {tuple(w_codes.shape)} do not match K={K}")
+    if w_gs.numel() not in (1, N // 128):
+        raise ValueError("nvfp4_linear: w_gs holds one scale, or one per 128-row block")
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8:
+        x2 = x2.contiguous()
+    a = quantize(x2)
+    w = NVFP4Tensor(w_codes, w_sf, w_gs, N, K, per_block=w_gs.numel() > 1)
+    xa = lb = None
+    if lora_A is not None:
+        if lora_B is None:
+            raise ValueError("nvfp4_linear: lora_A needs lora_B")
+        r = lora_A.shape[0]
+        scale = (lora_col_scale.float() * lora_scale if lora_col_scale is not None
+                 else torch.full((r,), float(lora_scale), dtype=torch.float32, device=x.device))
+        xa = lora_down(x2, lora_A, scale, a, w)
+        lb = lora_B.contiguous()
+    res2 = residual.reshape(-1, N) if residual is not None else None
+    gate2, gate_rows = None, 1
+    if gate is not None:
+        gate2 = gate.reshape(-1, N)
+        if x2.shape[0] % gate2.shape[0]:
+            raise ValueError("nvfp4_linear: gate rows must divide the rows of x")
+        gate_rows = x2.shape[0] // gate2.shape[0]
+    y = gemm(a, w, bias=bias, residual=res2, gate=gate2, gate_rows=gate_rows, lora_xa=xa, lora_b=lb)
+    return y.reshape(*x.shape[:-1], N)
+
+
+@nvfp4_linear.register_fake
+def _nvfp4_linear_fake(x, w_codes, w_sf, w_gs, bias=None, lora_A=None, lora_B=None, lora_scale=1.0,
+                       residual=None, gate=None, lora_col_scale=None):
+    return x.new_empty((*x.shape[:-1], w_codes.shape[0]), dtype=torch.bfloat16)
