@@ -3,7 +3,9 @@
 The ring's compute (StreamPipeline on a GPU) is replaced by a fake pipeline that finishes
 deterministic latents and records shared-curve updates, so the test covers exactly the
 multi-process part: slot ownership, curve broadcast tagged with the tick (applied on every
-rank at tag + 2) and the gather of finished latents to rank 0 in rank order.
+rank at tag + 2), the hot-LoRA (factors, strength, removal) and channel-gain broadcasts that
+switch on the same tick on every rank, the gather of finished latents to rank 0 in rank
+order, and the detection of a rank that left.
 """
 import os
 import socket
@@ -145,3 +147,85 @@ def test_sharded_ring_rank_failure_is_detected():
     assert res[0][0].startswith("error"), res[0]
     assert res[0][1] == 3  # the first tick after the peer left
     assert procs[1].exitcode == 3
+
+
+class FakeLoRAPipe(FakePipe):
+    """FakePipe that also records, at every tick, the channel gain and the LoRA banks of two
+    NVFP4 linears (the banks are host bookkeeping: no kernel runs on the CPU)."""
+
+    def __init__(self, rank, lins):
+        super().__init__(rank)
+        self.lins, self.gain, self.log = lins, None, []
+
+    def set_channel_gain_tensor(self, g):
+        self.gain = None if g is None else g.clone()
+
+    def tick_many(self):
+        banks = {n: sorted((i, e.strength, float(e.A.float().sum()), float(e.B.float().sum()))
+                           for i, e in lin.lora.entries.items()) for n, lin in self.lins.items()}
+        self.log.append((self.t, None if self.gain is None else float(self.gain.float().sum()), banks))
+        return super().tick_many()
+
+
+def _lora_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from demon_b200.nvfp4 import NVFP4Linear
+    from demon_b200.ring import ShardedRing
+    lins = {"layers.0.self_attn.q_proj.weight": NVFP4Linear(128, 256, bias=False, device="cpu"),
+            "layers.0.mlp.down_proj.weight": NVFP4Linear(256, 128, bias=False, device="cpu")}
+    pipe = FakeLoRAPipe(rank, lins)
+    ring = ShardedRing(pipe, rank, world, T, "cpu", curve_names=["velocity_scale"], curve_every=4,
+                       max_finished=2, lora_targets=lins)
+    g = torch.Generator().manual_seed(9)
+    pairs = {"layers.0.self_attn.q_proj.weight": (torch.randn(16, 128, generator=g), torch.randn(256, 16, generator=g)),
+             "layers.0.mlp.down_proj.weight": (torch.randn(32, 256, generator=g), torch.randn(128, 32, generator=g))}
+    gain = torch.rand(1, T, 64, generator=g) + 0.5
+    for t in range(16):
+        if rank == 0 and t == 1:
+            ring.enable_lora("L1", pairs, strength=0.5)
+        if rank == 0 and t == 5:
+            ring.set_channel_gain(gain)
+            ring.set_lora_strength("L1", 1.0)
+        if rank == 0 and t == 9:
+            ring.disable_lora("L1")
+            ring.set_channel_gain(None)
+        ring.step()
+    q.put((rank, pipe.log))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_ring_broadcasts_lora_and_gain():
+    """Rank 0's hot-LoRA enable (factors broadcast), strength change, removal and channel-gain
+    changes reach rank 1 and switch on the same tick on both ranks (announced with the next
+    control broadcast every 4 ticks, applied 2 ticks later), with identical factors."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lora_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, log = q.get(timeout=120)
+        res[r] = log
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0] == res[1]                     # same state at every tick on both ranks
+    by_t = {t: (gain, banks) for t, gain, banks in res[0]}
+    qn = "layers.0.self_attn.q_proj.weight"
+    for t in range(16):
+        gain, banks = by_t[t]
+        ids = [e[:2] for e in banks[qn]]
+        if t < 6:        # enable queued at tick 1, announced at 4, applied at 6
+            assert ids == [] and gain is None, t
+        elif t < 10:     # strength and gain queued at 5, announced at 8, applied at 10
+            assert ids == [("L1", 0.5)] and gain is None, t
+        elif t < 14:     # removal and gain clear queued at 9, announced at 12, applied at 14
+            assert ids == [("L1", 1.0)] and gain is not None, t
+        else:
+            assert ids == [] and gain is None, t
+    assert [e[0] for e in by_t[7][1]["layers.0.mlp.down_proj.weight"]] == ["L1"]
