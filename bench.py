@@ -672,36 +672,112 @@ def run_config3(dit, dev, ticks=24, warmup=24):
             "value": 1e3 / ms, "unit": "ticks/s", "ms_per_tick": ms, "ticks": ticks}
 
 
-def gemm_roofline(dit, dev, B):
-    """Device time of every NVFP4 GEMM of one eager DiT forward at batch B (CUDA events around
-    each launch on the launching stream): algorithmic FLOPs / summed GEMM time."""
+PHASE_FUNCS = (("Q", "gemm", "gemm"), ("D", "_attention", "attention"), ("D", "adanorm_quantize", "row_kernels"),
+               ("Q", "quantize", "row_kernels"), ("D", "head_norm_rope", "row_kernels"),
+               ("D", "silu_mul_quantize", "row_kernels"), ("Q", "bf16_linear", "bf16_linears"),
+               ("Q", "lora_down", "lora_down"))
+
+
+def _graph_ms(fn, reps=3):
+    """Device ms of fn() captured in one CUDA graph and replayed (CUDA events around the last
+    replay): no host launch gaps inside."""
+    import torch
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        fn()
+    for _ in range(reps - 1):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    del gr
+    return ms
+
+
+def forward_inputs(dev, B, T=None, L=None, seed=3):
+    import torch
+    T, L = T or T5, L or L5
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(B, T, 64, generator=g, device=dev).to(torch.bfloat16)
+    ctx = torch.randn(B, T, 128, generator=g, device=dev).to(torch.bfloat16)
+    enc = torch.randn(B, L, 2048, generator=g, device=dev).to(torch.bfloat16)
+    t = torch.full((B,), 0.5, device=dev, dtype=torch.bfloat16)
+    return dict(hidden_states=x, timestep=t, timestep_r=t, encoder_hidden_states=enc, context_latents=ctx)
+
+
+def forward_phases(dit, dev, B, T=None, L=None):
+    """Device time of one DiT forward at batch B split by kernel class, without host gaps.
+
+    One eager forward records the calls of each class (the function and its arguments) made by
+    layers 0 and 1 (one sliding-window and one full-attention layer; every other layer repeats
+    one of them with other weights) and outside the layer loop (embeddings, the encoder K/V of
+    all layers, the output projection).  Each class's recorded calls are then captured alone,
+    in order, into a CUDA graph and replayed between CUDA events; the in-layer part counts
+    num_layers / 2 times.  The whole forward is captured and timed the same way; ``other`` is
+    the forward minus the classes (PyTorch glue: concatenations, the AdaLN table sums).  The
+    GEMM class gives the roofline: algorithmic FLOPs / its device time."""
     import torch
     from demon_b200 import dit as D
-    orig = D.Q.gemm
+    Q = D.Q
+    mods = {"Q": Q, "D": D}
+    kw = forward_inputs(dev, B, T, L)
+    n_layers = len(dit.layers)
+    rep = n_layers / 2.0
     rec = []
-
-    def timed(a, w, *args, **kw):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        out = orig(a, w, *args, **kw)
-        e1.record()
-        rec.append((2.0 * a.rows * w.rows * a.K, e0, e1, (a.rows, w.rows, a.K)))
-        return out
-    g = torch.Generator(device=dev).manual_seed(3)
-    x = torch.randn(B, T5, 64, generator=g, device=dev).to(torch.bfloat16)
-    ctx = torch.randn(B, T5, 128, generator=g, device=dev).to(torch.bfloat16)
-    enc = torch.randn(B, L5, 2048, generator=g, device=dev).to(torch.bfloat16)
-    t = torch.full((B,), 0.5, device=dev, dtype=torch.bfloat16)
+    state = {"layer": None, "count": 0}
     with torch.no_grad():
-        dit(hidden_states=x, timestep=t, timestep_r=t, encoder_hidden_states=enc, context_latents=ctx)
-        D.Q.gemm = timed
+        dit(**kw)
+        torch.cuda.synchronize()
+        saved = []
+        for m, name, cls in PHASE_FUNCS:
+            mod = mods[m]
+            orig = getattr(mod, name)
+            saved.append((mod, name, orig))
+
+            def wrap(*a, _orig=orig, _cls=cls, **k):
+                out = _orig(*a, **k)
+                if state["layer"] is None or state["layer"] < 2:
+                    rec.append((_cls, _orig, a, k, 1.0 if state["layer"] is None else rep))
+                return out
+            setattr(mod, name, wrap)
+        layer_fwd = D.DiTLayer.forward
+
+        def layer_wrap(self, *a, **k):
+            state["layer"] = state["count"]
+            state["count"] += 1
+            try:
+                return layer_fwd(self, *a, **k)
+            finally:
+                state["layer"] = None
+        D.DiTLayer.forward = layer_wrap
         try:
-            dit(hidden_states=x, timestep=t, timestep_r=t, encoder_hidden_states=enc, context_latents=ctx)
+            dit(**kw)
         finally:
-            D.Q.gemm = orig
-    torch.cuda.synchronize()
-    flops = sum(r[0] for r in rec)
-    ms = sum(r[1].elapsed_time(r[2]) for r in rec)
+            for mod, name, orig in saved:
+                setattr(mod, name, orig)
+            D.DiTLayer.forward = layer_fwd
+        torch.cuda.synchronize()
+        ms = {"forward": _graph_ms(lambda: dit(**kw))}
+        for cls in dict.fromkeys(r_[0] for r_ in rec):
+            total = 0.0
+            for w in (1.0, rep):
+                calls = [(f, a, k) for c, f, a, k, w_ in rec if c == cls and w_ == w]
+                if not calls:
+                    continue
+
+                def replay(calls=calls):
+                    for f, a, k in calls:   # each output is dropped at once: the graph pool reuses it
+                        f(*a, **k)
+                total += w * _graph_ms(replay)
+            ms[cls] = total
+    gemms = [(a[0].rows, a[1].rows, a[0].K, k.get("silu_mul", False), w) for c, f, a, k, w in rec if c == "gemm"]
+    del rec
+    flops = sum(w * 2.0 * m * n * kk for m, n, kk, _, w in gemms)
+    ms["other"] = max(0.0, ms["forward"] - sum(v for c, v in ms.items() if c != "forward"))
     # DRAM traffic of the forward's GEMMs: ncu's per-launch bytes at M=12000 for each (N, K),
     # scaled by the launch's rows; launches of other shapes are counted in traffic_flops_covered
     traffic, covered = None, 0.0
@@ -709,14 +785,66 @@ def gemm_roofline(dit, dev, B):
     if tf.exists():
         per = json.loads(tf.read_text()).get("gemm_M12000", {})
         traffic = 0.0
-        for fl, _, _, (m, n, k) in rec:
-            b = per.get(f"{n}x{k}")
-            if b is not None:
-                traffic += b * m / 12000.0
-                covered += fl
-    alg = sum(m * k * 0.5625 + n * k * 0.5625 + m * n * 2 for _, _, _, (m, n, k) in rec)
-    return {"launches": len(rec), "flops": flops, "ms": ms, "achieved": flops / (ms * 1e-3) / 1e12,
-            "alg_bytes": alg, "traffic": traffic, "traffic_flops_covered": covered / flops if flops else 0.0}
+        for m, n, kk, _, w in gemms:
+            b_ = per.get(f"{n}x{kk}")
+            if b_ is not None:
+                traffic += w * b_ * m / 12000.0
+                covered += w * 2.0 * m * n * kk
+    alg = sum(w * (m * kk * 0.5625 + n * kk * 0.5625 + m * (n // 2 if sm else n) * 2) for m, n, kk, sm, w in gemms)
+    return {"ms": ms, "gemm_launches": sum(w for *_, w in gemms), "gemm_flops": flops,
+            "gemm_achieved": flops / (ms["gemm"] * 1e-3) / 1e12, "alg_bytes": alg, "traffic": traffic,
+            "traffic_flops_covered": covered / flops if flops else 0.0,
+            "method": "per kernel class: the recorded calls of layers 0-1 (x num_layers/2) and outside the "
+                      "layer loop, each class captured alone in a CUDA graph and replayed (CUDA events)"}
+
+
+def tick_phases(r, n=8):
+    """Mean device ms per tick of each part of a ring tick over n ticks (CUDA events on the
+    launching stream around the decoder forward -- a CUDA-graph replay --, the fused ODE step,
+    the finished-latent gather and the control broadcast; the GPU is busy with the forward when
+    the ODE and collective events are recorded, so host gaps do not enter them).  A collective's
+    time includes waiting for the slowest rank."""
+    import torch
+    from demon_b200 import ode as O
+    acc = {"forward": [], "ode_step": [], "gather": [], "broadcast": []}
+    pending = []
+
+    def timed(key, fn):
+        def f(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(*a, **k)
+            e1.record()
+            pending.append((key, e0, e1))
+            return out
+        return f
+    pipe, ring = r.pipe, r.ring
+    saved = [(pipe, "_forward"), (ring, "gather_finished"), (ring, "broadcast_curves")]
+    origs = [getattr(o, nm) for o, nm in saved]
+    ode_step = O.OdeTick.step
+    try:
+        pipe._forward = timed("forward", origs[0])
+        ring.gather_finished = timed("gather", origs[1])
+        ring.broadcast_curves = timed("broadcast", origs[2])
+        O.OdeTick.step = timed("ode_step", ode_step)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(n):
+            r.tick()
+        t1.record()
+        torch.cuda.synchronize()
+    finally:
+        for (o, nm), f in zip(saved, origs):
+            if o.__dict__.get(nm) is not None:
+                del o.__dict__[nm]
+        O.OdeTick.step = ode_step
+    for key, e0, e1 in pending:
+        acc[key].append(e0.elapsed_time(e1))
+    out = {k: sum(v) / n for k, v in acc.items()}
+    out["tick"] = t0.elapsed_time(t1) / n
+    out["other"] = max(0.0, out["tick"] - sum(out[k] for k in acc))
+    return out
 
 
 def count_launches(fn):
@@ -746,20 +874,164 @@ def count_launches(fn):
     return sum(counts.values()), counts
 
 
-def cpu_stream_sample(budget_s: float, layers: int = 2):
-    """The reference's CPU path for one slot of the tick: `layers` DiT layers of the CFG pair
-    (B=2, 750 tokens) on the CPU restatement of AceStepDiTModel (oracle/dit_ref.py) plus the
-    CPU ODE-step oracle on [1500, 64]; returns seconds per slot-step (24 layers + ODE)."""
+def lora_pairs(dit, dev, rank=64, seed=21, std=0.01):
+    """BASELINE config 4's hot LoRA: rank 64, A ~ N(0, 0.01), B ~ N(0, 0.01) (bf16, PEFT
+    layout) on every attention q/k/v/o (self and cross) and MLP linear of the DiT."""
+    import torch
+    from demon_b200.lora import lora_param_names
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = {}
+    for name, lin in lora_param_names(dit).items():
+        if ".self_attn." in name or ".cross_attn." in name or ".mlp." in name:
+            A = (torch.randn(rank, lin.in_features, generator=g, device=dev) * std).to(torch.bfloat16)
+            B = (torch.randn(lin.out_features, rank, generator=g, device=dev) * std).to(torch.bfloat16)
+            out[name] = (A, B)
+    return out
+
+
+def lora_flop_share(pairs, rows, enc_rows):
+    """LoRA FLOPs of one forward / its base NVFP4 GEMM FLOPs: 2 M r (K + N) against 2 M N K per
+    linear (M = the forward's token rows, or the encoder rows for the cross-attention K / V)."""
+    base = extra = 0.0
+    for name, (A, B) in pairs.items():
+        r, K = A.shape
+        N = B.shape[0]
+        M = enc_rows if (".cross_attn.k_proj" in name or ".cross_attn.v_proj" in name) else rows
+        base += 2.0 * M * N * K
+        extra += 2.0 * M * r * (K + N)
+    return extra / base
+
+
+def run_config2(dit, dev):
+    """one DiT decoder forward, batch 8 (ring depth 4 x CFG pair), T = 750
+    latent frames (375 tokens), text [256, 2048]: the forward as a CUDA-graph replay, with its
+    per-class split and GEMM throughput."""
+    fp = forward_phases(dit, dev, 8, T=750, L=L5)
+    ms = fp["ms"]["forward"]
+    return {"workload": "configs[1]: DiT decoder forward, batch 8 (depth 4 x CFG 2), T=750 (375 tokens), "
+                        "text [256,2048], all linears NVFP4, random init",
+            "ms_per_forward": ms, "forwards_per_s": 1e3 / ms, "gemm_ms": fp["ms"]["gemm"],
+            "gemm_tflops": fp["gemm_achieved"], "gemm_flops": fp["gemm_flops"],
+            "phases_ms": {k: round(v, 4) for k, v in fp["ms"].items()}}
+
+
+def run_config4(dit, dev, sweep=32):
+    """the hot-LoRA stream.  A depth-8 ring at T = 750 (375 tokens) of
+    standard-CFG requests on the DiT with a rank-64 LoRA (A, B ~ N(0, 0.01)) on every attention
+    q/k/v/o and MLP linear, enabled at strength 0 while the ring runs, swept 0 -> 1 over 32
+    ticks (each tick's strength a kernel scalar; the first non-zero one switches the fused
+    projections to per-linear GEMMs and re-captures the decoder graph), then removed (the
+    fused graph comes back).  Returns ticks/s of each phase and the LoRA FLOP share."""
+    import torch
+    from demon_b200.stream import SlotCondition, SlotRequest, StreamConfig, StreamPipeline
+    from demon_b200.lora import apply_to_decoder, drop_lora, lora_param_names
+    T, depth = 750, 8
+    g = torch.Generator().manual_seed(44)
+    bf = torch.bfloat16
+    ones = torch.ones(1, L5, dtype=bf, device=dev)
+    reqs = [SlotRequest(encoder_hidden_states=torch.randn(1, L5, 2048, generator=g).to(bf).to(dev),
+                        encoder_attention_mask=ones, context_latents=torch.randn(1, T, 128, generator=g).to(bf).to(dev),
+                        seed=900 + k, neg_conditions=[SlotCondition(torch.randn(1, L5, 2048, generator=g).to(bf).to(dev),
+                                                                    ones)],
+                        guidance_curve=torch.tensor(float(torch.rand(1, generator=g)) * 4 + 3)) for k in range(8)]
+    pipe = StreamPipeline(dit, StreamConfig(infer_steps=8), pipeline_depth=depth, device=dev, use_graphs=True)
+    n = [0]
+
+    def run_ticks(k, strength_at=None):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(k):
+            if strength_at is not None:
+                s_ = strength_at(i)
+                for name in pairs:
+                    lins[name].lora.set_strength("sweep", s_)
+            pipe.submit(reqs[n[0] % len(reqs)])
+            n[0] += 1
+            pipe.tick()
+        e1.record()
+        torch.cuda.synchronize()
+        return k / (e0.elapsed_time(e1) * 1e-3)
+    pairs, lins = {}, {}
+    run_ticks(depth + 8)                               # fill + capture the fused graph
+    base = run_ticks(16)
+    pairs = lora_pairs(dit, dev)
+    lins = lora_param_names(dit)
+    apply_to_decoder(dit, pairs, [("sweep", True, 0.0, pairs)], linears=lins)   # enabled at strength 0
+    at_zero = run_ticks(8)                             # contributes nothing: the fused graph stays
+    gen0 = pipe.decoder._gen
+    first = run_ticks(1, lambda i: 1.0 / sweep)        # first non-zero strength: re-capture
+    recaptured = pipe.decoder._gen != gen0
+    rest = run_ticks(sweep - 1, lambda i: (i + 2) / sweep)   # in-place strength updates: replays
+    drop_lora(lins, "sweep")                           # the enable / remove cycle ends
+    run_ticks(1)                                       # re-capture of the fused graph
+    after = run_ticks(8)
+    share = lora_flop_share(pairs, 2 * depth * (T // 2), 2 * depth * L5)
+    pipe.close()
+    return {"workload": "configs[3]: depth-8 ring, T=750 (375 tokens), standard CFG, hot LoRA rank 64 "
+                        "(A, B ~ N(0,0.01)) on every attention q/k/v/o (self + cross) and MLP linear, strength "
+                        f"0 -> 1 over {sweep} ticks, one enable / remove cycle",
+            "base_ticks_per_s": base, "enabled_at_strength0_ticks_per_s": at_zero,
+            "first_nonzero_tick_ticks_per_s": first, "lora_ticks_per_s": rest,
+            "after_remove_ticks_per_s": after, "lora_linears": len(pairs), "lora_flop_share": share,
+            "graph_recaptured_on_first_nonzero": recaptured}
+
+
+def ring_lora_leg(r, dit, dev, dist_mod, ticks=8):
+    """A hot LoRA through the sharded ring at N GPUs: rank 0 enables config 4's rank-64 LoRA
+    (its A / B factors are broadcast to every rank), every rank applies it on the same tick,
+    ``ticks`` ticks are timed with it on (max over ranks), then rank 0 removes it."""
+    import torch
+    from demon_b200.lora import lora_param_names
+    ring = r.ring
+    pairs = lora_pairs(dit, dev) if r.rank == 0 else None
+    payload = sum(A.numel() + B.numel() for A, B in pairs.values()) * 2 if pairs else 0
+    if r.rank == 0:
+        ring.enable_lora("ring-lora", pairs, strength=1.0)
+    for _ in range(ring.curve_every + ring.apply_delay + 1):   # announce, land, apply, re-capture
+        r.tick()
+    torch.cuda.synchronize()
+    held = sum(1 for lin in lora_param_names(dit).values() if "ring-lora" in lin.lora.entries)
+    held_min = int(-max_over_ranks(-float(held), dist_mod, dev))
+    if dist_mod is not None:
+        dist_mod.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(ticks):
+        r.tick()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist_mod, dev)
+    if r.rank == 0:
+        ring.disable_lora("ring-lora")
+    for _ in range(ring.curve_every + ring.apply_delay + 1):
+        r.tick()
+    torch.cuda.synchronize()
+    left = sum(1 for lin in lora_param_names(dit).values() if "ring-lora" in lin.lora.entries)
+    return {"ticks_per_s": ticks / (ms * 1e-3), "ticks": ticks, "linears_with_lora_min_over_ranks": held_min,
+            "linears_with_lora_after_remove": left, "payload_bytes_broadcast": payload,
+            "note": "rank-64 LoRA on every attention and MLP linear enabled on rank 0 and broadcast (NCCL) "
+                    "to every rank with the ring's control broadcast; timed with it on"}
+
+
+def cpu_stream_sample(budget_s: float, max_steps: int | None = None, min_steps: int = 1):
+    """The reference's CPU path for whole slot-steps of the tick: one slot's CFG pair (B=2, 750
+    tokens) through all 24 layers of the CPU restatement of AceStepDiTModel (oracle/dit_ref.py,
+    bit-exact with the reference module; the 24 layers share two layers' weights, which changes
+    no arithmetic) and then the CPU ODE-step oracle on [1500, 64] (CFG, APG, curves, DCW),
+    repeated while the budget lasts (at least ``min_steps``, at most ``max_steps``).  Returns
+    the measured seconds per slot-step and the sample's size."""
     import numpy as np
     import torch
     from oracle.dit_ref import DiTRef
     from oracle import ode_oracle as OO
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    D = 2048
+    D, NL = 2048, 24
     g = torch.Generator().manual_seed(0)
     sd = {}
-    for i in range(layers):
+    for i in range(2):
         p = f"layers.{i}"
         for nm, shp in ((".self_attn.q_proj", (2048, D)), (".self_attn.k_proj", (1024, D)),
                         (".self_attn.v_proj", (1024, D)), (".self_attn.o_proj", (D, 2048)),
@@ -772,46 +1044,50 @@ def cpu_stream_sample(budget_s: float, layers: int = 2):
         for nm in (".self_attn.q_norm", ".self_attn.k_norm", ".cross_attn.q_norm", ".cross_attn.k_norm"):
             sd[p + nm + ".weight"] = torch.ones(128, dtype=torch.bfloat16)
         sd[p + ".scale_shift_table"] = (torch.randn(1, 6, D, generator=g) / D ** 0.5).to(torch.bfloat16)
-    ref = DiTRef(sd, {"num_hidden_layers": layers, "sliding_window": 128})
+    for i in range(2, NL):
+        for k in [k for k in sd if k.startswith(f"layers.{i % 2}.")]:
+            sd[f"layers.{i}." + k.split(".", 2)[2]] = sd[k]
+    ref = DiTRef(sd, {"num_hidden_layers": NL, "sliding_window": 128})
     S = T5 // 2
-    h = torch.randn(2, S, D, generator=g).to(torch.bfloat16)
+    h0 = torch.randn(2, S, D, generator=g).to(torch.bfloat16)
     tproj = (torch.randn(2, 6, D, generator=g) * 0.1).to(torch.bfloat16)
     enc = torch.randn(2, L5, D, generator=g).to(torch.bfloat16)
     rope = ref.rope(S, torch.bfloat16)
     masks = [ref.mask4d(S, torch.bfloat16, 128), ref.mask4d(S, torch.bfloat16, None)]
     menc = ref.mask4d(max(S, L5), torch.bfloat16, None)[:, :, :S, :L5]
-    with torch.no_grad():
-        ref.layer(0, h, tproj, enc, rope, masks[0], menc)  # warm-up
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            for i in range(layers):
-                h = ref.layer(i, h, tproj, enc, rope, masks[i % 2], menc)
-                n += 1
-            if time.perf_counter() - t0 >= budget_s / 2:
-                break
-        t_layer = (time.perf_counter() - t0) / n
-    # one slot's ODE step (CFG, curves, mask) on the CPU oracle
     rng = np.random.default_rng(0)
     lat = lambda: rng.standard_normal((T5, 64)).astype(np.float32)
     slot = dict(xt=lat(), pos=[(lat(), None)], neg=[(lat(), None)], momentum=lat(), has_cfg=True,
                 rcfg_mode=None, guidance=np.full(T5, 5.0, np.float32), apg_momentum=-0.75, cfg_rescale=None,
                 velocity_scale=np.ones(T5, np.float32), t_curr=0.75, t_next=0.5, step_idx=3, total_steps=8,
                 infer_method="ode", noise=None, dec_next=True, dcw=("double", 0.05, 0.02))
-    t1 = time.perf_counter()
-    nodes = 0
-    try:
-        while time.perf_counter() - t1 < min(2.0, budget_s / 4) or nodes == 0:
-            OO.step_slot(dict(slot))
-            nodes += 1
-        t_ode = (time.perf_counter() - t1) / nodes
-        ode_note = "ode_oracle.step_slot"
-    except Exception as e:  # the oracle's slot dict needs more fields: count the DiT part only
-        t_ode = 0.0
-        ode_note = f"ODE oracle not timed ({type(e).__name__})"
-    per_slot = 24 * t_layer + t_ode
-    return {"per_slot_step_s": per_slot, "t_layer_s": t_layer, "t_ode_s": t_ode, "layers_timed": n,
-            "cores": cores, "ode": ode_note}
+
+    def slot_step():
+        h = h0
+        for i in range(NL):
+            h = ref.layer(i, h, tproj, enc, rope, masks[i % 2], menc)
+        OO.step_slot(dict(slot))
+        return h
+    with torch.no_grad():
+        ref.layer(0, h0, tproj, enc, rope, masks[0], menc)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            slot_step()
+            n += 1
+            el = time.perf_counter() - t0
+            if n >= min_steps and (el >= budget_s or (max_steps and n >= max_steps)):
+                break
+    return {"per_slot_step_s": el / n, "slot_steps": n, "seconds": el, "cores": cores,
+            "sample": f"{n} complete slot-steps ({NL} DiT layers of one slot's CFG pair, B=2, 750 tokens, on "
+                      f"the CPU restatement of AceStepDiTModel, bit-exact with the reference module, + the CPU "
+                      f"ODE-step oracle) in {el:.1f} s on {cores} cores, {el / n:.2f} s each; a tick is {RING} "
+                      f"slot-steps, so ticks/s = 1 / ({RING} x seconds per slot-step)"}
+
+
+def stream_config(world):
+    """The config dict of the stream workload, printed identically by both arms."""
+    return dict(CONFIG5, parallelism=f"slot-sharded ring x{world} ({RING // world} slots per GPU)",
+                prefill_ticks=STEPS5)
 
 
 def run_stream(args):
@@ -870,25 +1146,28 @@ def run_stream(args):
     for _ in range(2):
         r.tick(to_host)
     e2e_ms = timed(args.steps, to_host)
+    r.set_templates(tm_dev)
     status = nat.device_status()
-    groof = gemm_roofline(dit, dev, B=r.local)
-    groof_max = max_over_ranks(groof["ms"], dist_mod, dev)
+    # where a tick's time goes on this rank (then max over ranks per phase)
+    tp = tick_phases(r, n=8)
+    tp_max = {k: max_over_ranks(v, dist_mod, dev) for k, v in tp.items()}
+    fp = forward_phases(dit, dev, B=2 * r.local)
+    fp_max = {k: max_over_ranks(v, dist_mod, dev) for k, v in fp["ms"].items()}
+    lora_ring = ring_lora_leg(r, dit, dev, dist_mod)
     if rank == 0:
         pk = peaks()
         quant = measure_quantize_big(dev, stream, M=2 * r.local * (T5 // 2))
         odek = measure_ode(dev, stream) if args.ode else None
         lin = linear_leg(dev, stream)
         cfg3 = run_config3(dit, dev) if world == 1 else None
+        cfg2 = run_config2(dit, dev) if world == 1 else None
+        cfg4 = run_config4(dit, dev) if world == 1 else None
         cpu = None
         if world == 1 and args.cpu_seconds > 0:
             c = cpu_stream_sample(args.cpu_seconds)
             cpu = {"value": 1.0 / (RING * c["per_slot_step_s"]), "unit": "ticks/s", "cores": c["cores"],
-                   "kind": "port",
-                   "sample": f"{c['layers_timed']} DiT layers of one slot's CFG pair (B=2, 750 tokens) on the CPU "
-                             f"restatement of AceStepDiTModel (oracle/dit_ref.py, bit-exact with the reference "
-                             f"module) at {c['t_layer_s'] * 1e3:.0f} ms/layer, + {c['ode']} "
-                             f"({c['t_ode_s'] * 1e3:.1f} ms/slot), scaled to 24 layers x 64 slots per tick"}
-        achieved = groof["achieved"]
+                   "kind": "port", "sample": c["sample"], "extrapolated": True, "scale_factor": RING}
+        achieved = fp["gemm_achieved"]
         fp4_peak = 4.0 * pk.get("bf16_sustained", pk["bf16_tflops"])
         new_bytes = 2 * L5 * 2048 * 2 + T5 * 128 * 2
         line = {
@@ -896,22 +1175,28 @@ def run_stream(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4 linears (e2m1 x ue4m3 blocks, fp32 accumulate), bf16 elsewhere",
             "data": "synthetic (random-init weights, N(0,1) inputs)",
-            "config": dict(CONFIG5, parallelism=f"slot-sharded ring x{world} ({RING // world} slots per GPU)",
-                           prefill_ticks=STEPS5),
+            "config": stream_config(world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                         "frac": achieved / fp4_peak, "traffic": groof["traffic"],
+                         "frac": achieved / fp4_peak, "traffic": fp["traffic"],
                          "traffic_note": "DRAM bytes of all GEMM launches of one forward: ncu "
                                          "dram__bytes_read+write per launch at M=12000 for each (N, K), scaled "
                                          "by the launch's rows (profiles/traffic.json); covers "
-                                         f"{100 * groof['traffic_flops_covered']:.1f} % of the GEMM FLOPs; "
+                                         f"{100 * fp['traffic_flops_covered']:.1f} % of the GEMM FLOPs; "
                                          "algorithmic bytes (operands + bf16 outputs) "
-                                         f"{groof['alg_bytes'] / 1e9:.2f} GB",
+                                         f"{fp['alg_bytes'] / 1e9:.2f} GB",
                          "peak_note": "FP4 dense peak taken as 4x the measured sustained bf16 cuBLAS figure "
                                       f"({pk.get('bf16_sustained', pk['bf16_tflops']):.0f} TF/s, of measured: the "
                                       f"GEMMs run inside a long step); nominal 9 PF/s -> frac {achieved / 9000.0:.3f}",
                          "kernel": "demon::gemm_kernel (all NVFP4 GEMMs of one DiT forward at the rank's batch)",
-                         "gemm_launches": groof["launches"], "gemm_ms_per_forward": groof["ms"],
-                         "gemm_ms_per_forward_max_over_ranks": groof_max},
+                         "gemm_launches": fp["gemm_launches"], "gemm_ms_per_forward": fp["ms"]["gemm"],
+                         "gemm_ms_per_forward_max_over_ranks": fp_max["gemm"], "method": fp["method"]},
+            "phases": {"tick_ms": {k: round(v, 4) for k, v in tp.items()},
+                       "tick_ms_max_over_ranks": {k: round(v, 4) for k, v in tp_max.items()},
+                       "forward_ms": {k: round(v, 4) for k, v in fp["ms"].items()},
+                       "forward_ms_max_over_ranks": {k: round(v, 4) for k, v in fp_max.items()},
+                       "note": "tick: CUDA events around the graph-replayed forward, the ODE launch, the gather "
+                               "and the control broadcast over 8 ticks (collectives include waiting for the "
+                               "slowest rank); forward: " + fp["method"]},
             "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "ticks/s",
                     "h2d_bytes_per_step": world * r.k_new * new_bytes,
                     "d2h_bytes_per_step": world * r.k_new * T5 * 64 * 2},
@@ -921,11 +1206,13 @@ def run_stream(args):
             "device_status": list(status),
             "kernels": {"quantize": dict(quant, peak=pk["hbm_gbs"], frac=quant["achieved"] / pk["hbm_gbs"]),
                         "nvfp4_linear_config1": lin},
+            "secondary": {"lora_through_ring": lora_ring},
         }
         if odek is not None:
             line["kernels"]["ode_step"] = dict(odek, peak=pk["hbm_gbs"], frac=odek["achieved"] / pk["hbm_gbs"])
-        if cfg3 is not None:
-            line["secondary"] = {"config3_stream": cfg3}
+        for k, v in (("config3_stream", cfg3), ("config2_forward", cfg2), ("config4_hot_lora", cfg4)):
+            if v is not None:
+                line["secondary"][k] = v
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -936,19 +1223,26 @@ def run_stream(args):
 
 
 def run_reference_stream(args):
+    """The reference arm: the reference's CPU path (its DiT forward and ODE step, restated
+    bit-exactly) on this host's cores, each step one complete slot-step; ticks/s is
+    extrapolated from the measured seconds per slot-step (a tick is 64 slot-steps)."""
     rank, world, _ = env_rank()
     if rank != 0:
         return
-    budget = max(2.0, min(120.0, 3.0 * args.steps))
-    c = cpu_stream_sample(budget)
+    c0 = time.perf_counter()
+    cpu_stream_sample(0.0, max_steps=max(1, min(args.warmup, 3)))        # warm-up slot-steps
+    c = cpu_stream_sample(150.0, max_steps=args.steps, min_steps=args.steps)
     v = 1.0 / (RING * c["per_slot_step_s"])
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "ticks/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG5,
-        "cpu_baseline": {"value": v, "unit": "ticks/s", "cores": c["cores"], "kind": "port",
-                         "sample": f"{c['layers_timed']} DiT layers (CFG pair, 750 tokens) of the CPU restatement of "
-                                   f"AceStepDiTModel + {c['ode']}, scaled to 24 layers x 64 slots per tick"},
+        "steps": c["slot_steps"], "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": stream_config(world),
+        "extrapolated": True, "scale_factor": RING,
+        "sampled": {"slot_steps": c["slot_steps"], "seconds": c["seconds"], "per_slot_step_s": c["per_slot_step_s"],
+                    "wall_s_incl_warmup": time.perf_counter() - c0},
+        "cpu_baseline": {"value": v, "unit": "ticks/s", "cores": c["cores"], "kind": "port", "sample": c["sample"],
+                         "extrapolated": True, "scale_factor": RING},
         "e2e": {"value": v, "unit": "ticks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

@@ -230,22 +230,34 @@ class LoRABank:
     entries: dict = field(default_factory=dict)
     _cat: tuple | None = None
 
-    def set(self, lora_id: str, A: torch.Tensor, B: torch.Tensor, strength: float = 1.0) -> None:
-        self.entries[lora_id] = _LoRAEntry(A.to(torch.bfloat16).contiguous(), B.to(torch.bfloat16).contiguous(),
-                                           float(strength))
+    @staticmethod
+    def _contributes(e) -> bool:
+        return e is not None and e.enabled and e.strength != 0.0
+
+    def _changed(self) -> None:
         self._cat = None
         bump_generation()
 
+    def set(self, lora_id: str, A: torch.Tensor, B: torch.Tensor, strength: float = 1.0) -> None:
+        """Register (or replace) a LoRA.  One that contributes nothing (strength 0) leaves the
+        concatenated operands, and so the captured graphs, as they are."""
+        old = self.entries.get(lora_id)
+        new = _LoRAEntry(A.to(torch.bfloat16).contiguous(), B.to(torch.bfloat16).contiguous(), float(strength))
+        self.entries[lora_id] = new
+        if self._contributes(old) or self._contributes(new):
+            self._changed()
+
     def remove(self, lora_id: str) -> None:
-        self.entries.pop(lora_id, None)
-        self._cat = None
-        bump_generation()
+        if self._contributes(self.entries.pop(lora_id, None)):
+            self._changed()
 
     def set_strength(self, lora_id: str, strength: float) -> None:
         e = self.entries[lora_id]
         old, new = e.strength, float(strength)
         e.strength = new
-        if self._cat is not None and self._cat[0] is not None and e.enabled and old != 0.0 and new != 0.0:
+        if old == new or not e.enabled or (old == 0.0 and new == 0.0):
+            return
+        if self._cat is not None and self._cat[0] is not None and old != 0.0 and new != 0.0:
             off = 0
             for x in self.entries.values():
                 if x is e:
@@ -254,13 +266,14 @@ class LoRABank:
                     off += x.A.shape[0]
             self._cat[2][off:off + e.A.shape[0]].fill_(new)   # same operands: graphs stay valid
             return
-        self._cat = None
-        bump_generation()
+        self._changed()
 
     def enable(self, lora_id: str, enabled: bool = True) -> None:
-        self.entries[lora_id].enabled = enabled
-        self._cat = None
-        bump_generation()
+        e = self.entries[lora_id]
+        was = self._contributes(e)
+        e.enabled = enabled
+        if was != self._contributes(e):
+            self._changed()
 
     def active(self):
         """(A_cat [R, K], B_cat [N, R], col_scale fp32 [R]) or None when no LoRA contributes."""
