@@ -289,9 +289,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0, it = 0;
       bool ok = true;
       for (int tile = cid; ok && tile < num_tiles; tile += ncl, ++it) {
-        // the epilogue must have drained the previous tile's accumulator
-        if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4, lim))) break;
-        tc_fence_after();
+        // the epilogue must have drained the previous tile's accumulator; without hot LoRA the
+        // first stage's scale-factor copies are issued before that wait
+        const bool early_sf = FP4 && lboxes == 0;
+        if (!early_sf) {
+          if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4, lim))) break;
+          tc_fence_after();
+        }
         uint32_t accum = 0;
         for (int b = 0; b < lboxes; ++b, ++g) {
           const int s = g % STAGES;
@@ -338,6 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                   tc_cp_32x128b_warpx4(tmem + C::kSfbCol + ((BN + 127) / 128) * 4 * j + 4 * h,
                                        sf_desc(sfb + h * 2048 + j * 512));
               }
+            }
+            if (early_sf && kt == 0) {
+              if (!(ok = mbar_wait(acc_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 4, lim))) break;
+              tc_fence_after();
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
