@@ -64,37 +64,30 @@ __host__ __device__ __forceinline__ int ode_rows_per_cta(int T, int cluster) {
 
 __device__ __forceinline__ float curve(const float* c, float s, int t) { return c ? __ldg(c + t) : s; }
 
-// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11) keyed by the slot seed;
-// counter = (element group, step).  Box-Muller turns it into 4 normals.
-__device__ __forceinline__ void philox_normal4(uint64_t seed, uint64_t step, uint64_t group, float (&z)[4]) {
-  uint32_t c0 = (uint32_t)group, c1 = (uint32_t)(group >> 32), c2 = (uint32_t)step, c3 = (uint32_t)(step >> 32);
-  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
-#pragma unroll
-  for (int i = 0; i < 10; ++i) {
-    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
-    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
-    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
-    c0 = n0;
-    c1 = lo1;
-    c2 = n2;
-    c3 = lo0;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
-  }
-  const uint32_t u[4] = {c0, c1, c2, c3};
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float u1 = __uint2float_rn(u[2 * i] >> 8) * 5.9604644775390625e-08f + 2.98023223876953125e-08f;
-    const float u2 = __uint2float_rn(u[2 * i + 1] >> 8) * 5.9604644775390625e-08f;
-    // hardware log / sqrt / sin / cos approximations: the draws are rounded to bf16 (8
-    // significant bits), far coarser than their error
-    float r;
-    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(-2.0f * __logf(u1)));
-    float s, c;
-    __sincosf(6.2831853071795865f * (u2 - 0.5f), &s, &c);  // a uniform angle in [-pi, pi)
-    z[2 * i] = rnd(r * c);
-    z[2 * i + 1] = rnd(r * s);
-  }
+// Per-step Gaussian noise, counter-based so that a slot's draws depend only on (seed, step,
+// element): the SplitMix64 output function (Vigna; Steele, Lea, Flood, OOPSLA'14) of
+// seed_key + counter * 0x9e3779b97f4a7c15 gives 64 uniform bits per counter, and Box-Muller
+// turns its two 32-bit halves into two normals.  The counter of an element pair is
+// step * 2^36 + (element index) / 2, distinct for every pair of every step of a slot.
+__device__ __forceinline__ uint64_t splitmix64_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t noise_key(uint64_t seed) { return splitmix64_mix(seed + 0x9e3779b97f4a7c15ull); }
+
+// two normals from the 64 bits of one counter
+__device__ __forceinline__ float2 normal2(uint64_t key, uint64_t counter) {
+  const uint64_t z = splitmix64_mix(key + counter * 0x9e3779b97f4a7c15ull);
+  const float u1 = __uint2float_rn((uint32_t)(z >> 40)) * 5.9604644775390625e-08f + 2.98023223876953125e-08f;
+  const float u2 = __uint2float_rn((uint32_t)(z >> 8) & 0xFFFFFFu) * 5.9604644775390625e-08f;
+  // hardware log / sqrt / sin / cos approximations: the draws are rounded to bf16 (8 significant
+  // bits), far coarser than their error
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(-2.0f * __logf(u1)));
+  float sn, cs;
+  __sincosf(6.2831853071795865f * (u2 - 0.5f), &sn, &cs);  // a uniform angle in [-pi, pi)
+  return make_float2(rnd(r * cs), rnd(r * sn));
 }
 
 struct OdeShared {
@@ -505,14 +498,10 @@ __global__ void __launch_bounds__(kOdeThreads, kOdeMinBlocks)
         words(ldg16(S.noise, off), ew);
 #pragma unroll
         for (int j = 0; j < 4; ++j) eps[j] = bf2_f2(ew[j]);
-      } else {  // counters: the channel quads' indices in the slot, (t * 64 + c) / 4
-        float z0[4], z1[4];
-        philox_normal4(S.seed, S.step, (uint64_t)off >> 2, z0);
-        philox_normal4(S.seed, S.step, ((uint64_t)off >> 2) + 1, z1);
-        eps[0] = make_float2(z0[0], z0[1]);
-        eps[1] = make_float2(z0[2], z0[3]);
-        eps[2] = make_float2(z1[0], z1[1]);
-        eps[3] = make_float2(z1[2], z1[3]);
+      } else {  // counters: the element pairs' indices in the slot, (t * 64 + c) / 2, per step
+        const uint64_t key = noise_key(S.seed), cbase = (S.step << 36) + ((uint64_t)off >> 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) eps[j] = normal2(key, cbase + j);
       }
     }
     uint32_t xn[4];

@@ -107,7 +107,7 @@ class SlotStep:
     mask: Optional[LatentMask] = None
     complex_extra: bool = False                    # extra conds / temporal weight / step range
     infer_method: str = "ode"
-    noise: Optional[torch.Tensor] = None           # explicit step noise (else in-kernel Philox)
+    noise: Optional[torch.Tensor] = None           # explicit step noise (else in-kernel counter-based noise)
     dec_out: Optional[torch.Tensor] = None         # next tick's decoder input row
     dcw: Optional[tuple] = None                    # active DCW corrector: (mode, scaler, high_scaler)
     seed: int = 0

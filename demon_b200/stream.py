@@ -16,7 +16,7 @@ signature (``demon_b200.dit.DemonDiT`` on B200).
 
 Noise: slot initial noise is drawn on the CPU exactly as the reference does
 (stream.py:403-451); per-step noise (SDE / ode_noise_curve) is drawn in the
-kernel with Philox keyed by (slot seed, step), so a slot's trajectory does
+kernel from a counter-based generator keyed by (slot seed, step), so a slot's trajectory does
 not depend on which other slots share its ticks.
 """
 from __future__ import annotations

@@ -293,13 +293,13 @@ typedef struct DemonOdeSlot {
   const void* mask_noise;                      /* [T, D] fixed mask noise */
   const void* source;                          /* [T, D] source latents (SDE curve) */
   const void* x0_target;                       /* [T, D] */
-  const void* noise;                           /* [T, D] step noise (NULL = in-kernel Philox) */
+  const void* noise;                           /* [T, D] step noise (NULL = in-kernel counter-based noise) */
   void* dec_out;                               /* [T, D] next decoder input */
   float mask_s_next;                           /* mask strength at the next step */
   float t_curr, t_next;
   int32_t flags;
-  uint64_t seed;                               /* Philox key for in-kernel noise */
-  uint64_t step;                               /* Philox counter offset (step index) */
+  uint64_t seed;                               /* key of the in-kernel noise */
+  uint64_t step;                               /* step index in the noise counter */
   /* DCW post-step correction (StreamPipeline._maybe_dcw, stream.py:1387-1405;
    * DCWCorrector.apply, dcw.py:428-490): band coefficients per haar band k = t / 2
    * ([ceil(T / 2)] fp32, the scaler curves already multiplied by t / (1 - t) and resampled),

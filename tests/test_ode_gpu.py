@@ -226,14 +226,14 @@ def test_ode_prepare_matches_oracle(cuda, n):
 
 
 def test_ode_in_kernel_noise_is_deterministic_and_gaussian(cuda):
-    """Philox noise: same seed/step -> identical bits; statistics of N(0,1)."""
+    """In-kernel noise: same seed/step -> identical bits; statistics of N(0,1)."""
     from demon_b200 import ode
     T = 1500
     outs = []
-    for _ in range(2):
+    for step in (3, 3, 4):
         xt = torch.zeros(T, D, dtype=torch.bfloat16, device=cuda)
         v = torch.zeros(T, D, dtype=torch.bfloat16, device=cuda)
-        st = ode.SlotStep(xt=xt, t_curr=1.0, t_next=0.5, step_idx=3, total_steps=8, pos=[(v, None)],
+        st = ode.SlotStep(xt=xt, t_curr=1.0, t_next=0.5, step_idx=step, total_steps=8, pos=[(v, None)],
                           infer_method="sde", seed=99)
         tick = ode.OdeTick(cuda, T, max_slots=1)
         tick.add(st)
@@ -242,6 +242,14 @@ def test_ode_in_kernel_noise_is_deterministic_and_gaussian(cuda):
     assert torch.equal(outs[0], outs[1])
     z = outs[0] / 0.5  # bare SDE: xt = t_next * noise + (1 - t_next) * 0
     assert abs(float(z.mean())) < 0.02 and abs(float(z.std()) - 1.0) < 0.02
+    # the two normals of one draw, neighbouring draws and the next step are uncorrelated
+    def corr(a, b):
+        a, b = a.flatten() - a.mean(), b.flatten() - b.mean()
+        return float((a * b).sum() / (a.norm() * b.norm()))
+    assert abs(corr(z[:, 0::2], z[:, 1::2])) < 0.02
+    assert abs(corr(z[:, 0:D - 2], z[:, 2:D])) < 0.02
+    assert abs(corr(z, outs[2] / 0.5)) < 0.02
+    assert abs(float((z ** 4).mean()) - 3.0) < 0.15   # Gaussian kurtosis
 
 
 def test_ode_rejects_bad_launches(cuda):
