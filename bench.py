@@ -1148,6 +1148,18 @@ def run_stream(args):
     e2e_ms = timed(args.steps, to_host)
     r.set_templates(tm_dev)
     status = nat.device_status()
+    if not args.legs:  # the timed stream only (the launch-list profile uses this form)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": args.steps / (ms * 1e-3), "unit": "ticks/s",
+                              "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": ms / args.steps, "e2e_ticks_per_s": args.steps / (e2e_ms * 1e-3),
+                              "config": stream_config(world), "note": "--no-legs: secondary legs skipped",
+                              "device_status": list(status)}), flush=True)
+        if dist_mod is not None:
+            r.pipe.decoder._graphs.clear()
+            dist_mod.barrier()
+            dist_mod.destroy_process_group()
+        return
     # where a tick's time goes on this rank (then max over ranks per phase)
     tp = tick_phases(r, n=8)
     tp_max = {k: max_over_ranks(v, dist_mod, dev) for k, v in tp.items()}
@@ -1324,6 +1336,8 @@ def main():
     ap.add_argument("--shape", default="12000,6144,2048", help="M,N,K[:M,N,K...] of --workload gemm")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-ode", dest="ode", action="store_false", help="skip the ODE-step roofline leg")
+    ap.add_argument("--no-legs", dest="legs", action="store_false",
+                    help="stream: time the stream and its e2e run only (no phase split, kernel or config legs)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = {"stream": 20, "linear": 2000}.get(args.workload, 10)
