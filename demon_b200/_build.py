@@ -23,7 +23,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OBJ = PKG / "_build"
 LIB = PKG / "libdemon_b200.so"
-SOURCES = ["capi.cu", "nvfp4_quant.cu", "nvfp4_gemm.cu", "ode_step.cu", "nvfp4_noalloc.cu", "dit_ops.cu"]
+SOURCES = ["capi.cu", "nvfp4_quant.cu", "nvfp4_gemm.cu", "ode_step.cu", "nvfp4_noalloc.cu", "dit_ops.cu",
+           "attention.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -42,6 +42,7 @@ EXPORTED = (
     "demon_ode_step", "demon_ode_prepare", "demon_ode_cluster_size", "demon_nvfp4_noalloc_scratch_bytes",
     "demon_nvfp4_linear_noalloc", "demon_test_arm_gemm_stall",
     "demon_bf16_linear", "demon_adanorm_quantize", "demon_silu_mul_quantize", "demon_head_norm_rope",
+    "demon_attention", "demon_attention_args_size",
 )
 
 _vp = ctypes.c_void_p
@@ -83,6 +84,17 @@ class DemonOdeSlot(ctypes.Structure):
         ("mask_s_next", _f32), ("t_curr", _f32), ("t_next", _f32), ("flags", _i32),
         ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64),
         ("dcw_lo", _vp), ("dcw_lo_s", _f32), ("dcw_hi", _vp), ("dcw_hi_s", _f32),
+    ]
+
+
+class DemonAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("ldq", _i64), ("sq", _i64),
+        ("k", _vp), ("ldk", _i64), ("sk", _i64),
+        ("v", _vp), ("ldv", _i64), ("sv", _i64),
+        ("o", _vp), ("ldo", _i64), ("so", _i64),
+        ("B", _i32), ("S", _i32), ("L", _i32), ("Hq", _i32), ("Hk", _i32), ("head_dim", _i32), ("window", _i32),
+        ("scale", _f32),
     ]
 
 
@@ -130,15 +142,19 @@ def load() -> ctypes.CDLL:
                                              _vp, _i64, _vp]
         L.demon_silu_mul_quantize.argtypes = [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp]
         L.demon_head_norm_rope.argtypes = [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _f32, _vp]
+        L.demon_attention.argtypes = [ctypes.POINTER(DemonAttnArgs), _vp]
         for name in EXPORTED:
-            getattr(L, name).restype = (_i64 if name in ("demon_nvfp4_sf_bytes", "demon_nvfp4_noalloc_scratch_bytes")
-                                        else ctypes.c_int)
+            getattr(L, name).restype = (_i64 if name in ("demon_nvfp4_sf_bytes", "demon_nvfp4_noalloc_scratch_bytes",
+                                                         "demon_attention_args_size") else ctypes.c_int)
         g, o = _i64(), _i64()
         L.demon_struct_sizes(ctypes.byref(g), ctypes.byref(o))
         if g.value != ctypes.sizeof(DemonGemmArgs) or o.value != ctypes.sizeof(DemonOdeSlot):
             raise RuntimeError(
                 f"ABI mismatch: C sizeof(DemonGemmArgs)={g.value} vs {ctypes.sizeof(DemonGemmArgs)}, "
                 f"sizeof(DemonOdeSlot)={o.value} vs {ctypes.sizeof(DemonOdeSlot)}")
+        if L.demon_attention_args_size() != ctypes.sizeof(DemonAttnArgs):
+            raise RuntimeError(f"ABI mismatch: C sizeof(DemonAttnArgs)={L.demon_attention_args_size()} vs "
+                               f"{ctypes.sizeof(DemonAttnArgs)}")
         _lib = L
     return _lib
 

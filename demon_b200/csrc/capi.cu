@@ -84,8 +84,7 @@ bool device_pending(const std::atomic<uint64_t>& flags) {
 
 void mark_device_done(std::atomic<uint64_t>& flags) { flags.fetch_or(device_bit(), std::memory_order_acq_rel); }
 
-int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
-                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -93,7 +92,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
         q == cudaDriverEntryPointSuccess)
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
-  if (!g_encode) {
+  return g_encode;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
+                 uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  if (!encoder()) {
     set_error("cuTensorMapEncodeTiled is unavailable from the driver");
     return DEMON_ERR_CUDA;
   }
@@ -112,6 +116,33 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d): dims %llux%llu ld %llu box %ux%u", (int)r,
               (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)ld_bytes, box_cols, box_rows);
+    return DEMON_ERR_INVALID;
+  }
+  return DEMON_OK;
+}
+
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t depth,
+                      uint64_t ld_bytes, uint64_t depth_bytes, uint32_t box_cols, uint32_t box_rows) {
+  if (!encoder()) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return DEMON_ERR_CUDA;
+  }
+  if (((uintptr_t)base & 15) != 0 || (ld_bytes & 15) != 0 || (depth_bytes & 15) != 0) {
+    set_error("TMA operand must be 16-byte aligned with 16-byte multiple pitches (ld=%llu, depth pitch=%llu)",
+              (unsigned long long)ld_bytes, (unsigned long long)depth_bytes);
+    return DEMON_ERR_INVALID;
+  }
+  const cuuint64_t dims[3] = {cols, rows, depth};
+  const cuuint64_t strides[2] = {ld_bytes, depth_bytes};
+  const cuuint32_t box[3] = {box_cols, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): dims %llux%llux%llu pitches %llu/%llu box %ux%u", (int)r,
+              (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)depth,
+              (unsigned long long)ld_bytes, (unsigned long long)depth_bytes, box_cols, box_rows);
     return DEMON_ERR_INVALID;
   }
   return DEMON_OK;

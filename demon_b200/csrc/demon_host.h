@@ -28,6 +28,11 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                  uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
+// 3-D bf16 tiled tensor map with 128-byte swizzle: `depth` blocks of `rows` x `cols`
+// elements (row pitch `ld_bytes`, block pitch `depth_bytes`), box `box_rows` x `box_cols` x 1.
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t depth,
+                      uint64_t ld_bytes, uint64_t depth_bytes, uint32_t box_cols, uint32_t box_rows);
+
 // Host-only argument checks of demon_nvfp4_quantize / demon_nvfp4_gemm (no CUDA call, no
 // launch): DEMON_OK, or DEMON_ERR_INVALID with the message set.  The entry points run them
 // first; callers that chain both kernels run both before launching either.

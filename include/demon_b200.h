@@ -332,6 +332,36 @@ DEMON_API int demon_ode_prepare(const DemonOdeSlot* slots_dev, int32_t n_slots, 
  */
 DEMON_API int demon_ode_cluster_size(int32_t n_slots, int64_t T, int32_t* cluster);
 
+/*
+ * Bidirectional grouped-query attention, head_dim 128, bf16:
+ *   o[b, i, h] = sum_j softmax_j(scale * q[b, i, h] . k[b, j, h / G]) v[b, j, h / G],
+ * G = Hq / Hk (even), j over all L keys, or over |i - j| <= window when window >= 0 (then
+ * S == L).  Element (b, i, h, d) of q sits at q + b * sq + i * ldq + h * 128 + d (pitches in
+ * elements; heads contiguous within a row), likewise k / v (Hk heads, L rows) and o (Hq heads,
+ * S rows); the q / k / v pitches of one fused projection output work as they are.
+ * Stands in for the attention interface call of AceStepAttention.forward
+ * (acestep/models/modeling_acestep_v15_turbo.py:358-372), the sliding-window band of
+ * lines 110-112 of the same file, with the GQA K / V heads shared instead of repeated.
+ * fp32 scores and softmax, bf16 probabilities into the P V product; each (sequence, head,
+ * query block) is computed from that sequence alone (no split over keys), so results do
+ * not depend on the batch.
+ */
+typedef struct DemonAttnArgs {
+  const void* q;
+  int64_t ldq, sq;
+  const void* k;
+  int64_t ldk, sk;
+  const void* v;
+  int64_t ldv, sv;
+  void* o;
+  int64_t ldo, so;
+  int32_t B, S, L, Hq, Hk, head_dim, window; /* window -1: no band */
+  float scale;                              /* softmax scale, e.g. 1 / sqrt(128) */
+} DemonAttnArgs;
+
+DEMON_API int demon_attention(const DemonAttnArgs* args, void* stream);
+DEMON_API int64_t demon_attention_args_size(void);
+
 #ifdef __cplusplus
 }
 #endif
