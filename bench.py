@@ -202,6 +202,114 @@ def run_reference(args):
 # kernel legs
 # ---------------------------------------------------------------------------
 
+class _CudnnBand:
+    """The library baseline the attention leg compares against for the sliding window: one
+    cuDNN-frontend fused-attention graph with a diagonal band (left bound window + 1, right
+    bound window), GQA native, reading q / k / v through their strides."""
+
+    def __init__(self):
+        self._graphs = {}
+        self._handle = None
+
+    def __call__(self, q, k, v, window):
+        import cudnn
+        import torch
+        B, S, Hq, D = q.shape
+        L, Hk = k.shape[1], k.shape[2]
+        out = torch.empty(B, S, Hq, D, dtype=torch.bfloat16, device=q.device)
+        qv, kv, vv, ov = (t.transpose(1, 2) for t in (q, k, v, out))
+        strides = tuple(tuple(t.stride()) for t in (qv, kv, vv, ov))
+        if self._handle is None:
+            self._handle = cudnn.create_handle()
+        key = (B, S, L, Hq, Hk, D, window, strides)
+        ent = self._graphs.get(key)
+        if ent is None:
+            c = cudnn
+            g = c.pygraph(io_data_type=c.data_type.BFLOAT16, intermediate_data_type=c.data_type.FLOAT,
+                          compute_data_type=c.data_type.FLOAT, handle=self._handle)
+            ts = [g.tensor(name=n, dim=[B, h, n_, D], stride=list(st), data_type=c.data_type.BFLOAT16)
+                  for n, h, n_, st in (("q", Hq, S, strides[0]), ("k", Hk, L, strides[1]), ("v", Hk, L, strides[2]))]
+            o, _ = g.sdpa(q=ts[0], k=ts[1], v=ts[2], is_inference=True, attn_scale=D ** -0.5,
+                          diagonal_band_left_bound=window + 1, diagonal_band_right_bound=window)
+            o.set_output(True).set_dim([B, Hq, S, D]).set_stride(list(strides[3])).set_data_type(c.data_type.BFLOAT16)
+            g.validate()
+            g.build_operation_graph()
+            g.create_execution_plans([c.heur_mode.A, c.heur_mode.FALLBACK])
+            g.check_support()
+            g.build_plans()
+            ws = torch.empty(max(1, g.get_workspace_size()), dtype=torch.uint8, device=q.device)
+            ent = self._graphs[key] = (g, ts + [o], ws)
+        g, (tq, tk, tv, to), ws = ent
+        cudnn.set_stream(handle=self._handle, stream=torch.cuda.current_stream().cuda_stream)
+        g.execute({tq: qv, tk: kv, tv: vv, to: ov}, ws, handle=self._handle)
+        return out
+
+
+def attention_leg(dev, B=128, S=750, L=L5, hq=16, hk=8, reps=20):
+    """The DiT's three attention classes at the tick's shapes (B = 2 CFG x 64 slots sequences of
+    750 tokens, GQA 16/8 x 128, text 256): demon's sm_100a kernel beside the cuDNN fused
+    attention it replaced (SDPA for global and cross, a diagonal-band graph for the window),
+    each replayed from a CUDA graph of `reps` launches.  FLOPs count only the scores inside the
+    band (4 * B * Hq * D per valid (query, key) pair)."""
+    import torch
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from demon_b200.attention import attention
+    D = 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(B * S, (hq + 2 * hk) * D, device=dev, generator=g).to(torch.bfloat16)
+    ld = qkv.stride(0)
+    q = qkv.as_strided((B, S, hq, D), (S * ld, ld, D, 1))
+    k = qkv.as_strided((B, S, hk, D), (S * ld, ld, D, 1), hq * D)
+    v = qkv.as_strided((B, S, hk, D), (S * ld, ld, D, 1), (hq + hk) * D)
+    kvx = torch.randn(B * L, 2 * hk * D, device=dev, generator=g).to(torch.bfloat16)
+    ldk = kvx.stride(0)
+    ck = kvx.as_strided((B, L, hk, D), (L * ldk, ldk, D, 1))
+    cv = kvx.as_strided((B, L, hk, D), (L * ldk, ldk, D, 1), hk * D)
+    qc = torch.randn(B, S, hq, D, device=dev, generator=g).to(torch.bfloat16)
+    band = _CudnnBand()
+
+    def sdpa(qq, kk, vv):
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            return torch.nn.functional.scaled_dot_product_attention(
+                qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2), enable_gqa=True).transpose(1, 2)
+    n_band = sum(min(i + 128, S - 1) - max(i - 128, 0) + 1 for i in range(S))
+    classes = {
+        "band": (lambda: attention(q, k, v, 128), lambda: band(q, k, v, 128), 4 * B * hq * n_band * D),
+        "global": (lambda: attention(q, k, v), lambda: sdpa(q, k, v), 4 * B * hq * S * S * D),
+        "cross": (lambda: attention(qc, ck, cv), lambda: sdpa(qc, ck, cv), 4 * B * hq * S * L * D),
+    }
+    res = {}
+    for name, (mine, lib, flops) in classes.items():
+        a, b = mine().float(), lib().float()
+        diff = float((a - b).norm() / b.norm())
+        t = {}
+        for tag, fn in (("demon", mine), ("cudnn", lib)):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(reps):
+                    fn()
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t[tag] = e0.elapsed_time(e1) * 1e3 / reps
+            del gr
+        res[name] = {"demon_us": round(t["demon"], 1), "cudnn_us": round(t["cudnn"], 1),
+                     "demon_tflops": round(flops / t["demon"] / 1e6, 1), "cudnn_tflops": round(flops / t["cudnn"] / 1e6, 1),
+                     "demon_over_cudnn_time": round(t["demon"] / t["cudnn"], 3), "rel_diff_vs_cudnn": diff}
+    per_fwd = {tag: 12 * res["band"][f"{tag}_us"] + 12 * res["global"][f"{tag}_us"] + 24 * res["cross"][f"{tag}_us"]
+               for tag in ("demon", "cudnn")}
+    res["per_forward_ms"] = {k: round(v / 1e3, 3) for k, v in per_fwd.items()}
+    res["shapes"] = f"B={B} sequences x {S} tokens, GQA {hq}/{hk} x 128, text {L}; 12 band + 12 global + 24 cross per forward"
+    return res
+
+
 def ode_workload(dev, nslots=64, T=1500, seed=0):
     """Config-3 slot features at config-5 scale: 64 slots x T=1500 x 64, CFG modes cycling
     standard / RCFG-initialize (cached negative) / RCFG-self, per-slot guidance U(3,7),
@@ -1171,6 +1279,7 @@ def run_stream(args):
         quant = measure_quantize_big(dev, stream, M=2 * r.local * (T5 // 2))
         odek = measure_ode(dev, stream) if args.ode else None
         lin = linear_leg(dev, stream)
+        attn = attention_leg(dev, B=2 * r.local)
         cfg3 = run_config3(dit, dev) if world == 1 else None
         cfg2 = run_config2(dit, dev) if world == 1 else None
         cfg4 = run_config4(dit, dev) if world == 1 else None
@@ -1217,7 +1326,7 @@ def run_stream(args):
             "clocks": clk.summary(),
             "device_status": list(status),
             "kernels": {"quantize": dict(quant, peak=pk["hbm_gbs"], frac=quant["achieved"] / pk["hbm_gbs"]),
-                        "nvfp4_linear_config1": lin},
+                        "nvfp4_linear_config1": lin, "attention": attn},
             "secondary": {"lora_through_ring": lora_ring},
         }
         if odek is not None:

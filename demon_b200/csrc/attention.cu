@@ -26,6 +26,8 @@
 // MMA order per unit with n key tiles (the S of one head is computed while the other head's
 // softmax runs):
 //   QK0(0) QK1(0) PV0(0) | for i >= 1: QK0(i) PV1(i-1) QK1(i) PV0(i) | PV1(n-1)
+// Each PV is issued in two halves of 64 keys: the softmax publishes the probabilities of keys
+// 0-63 first, and their product runs while it computes those of keys 64-127.
 // The commit that signals S_h(i) therefore also covers PV_h(i-1): when a softmax warp sees
 // S_h(i), no MMA touches O_h until it publishes P_h(i), so it may rescale O_h in place.
 //
@@ -56,15 +58,27 @@ constexpr int kD = 128;                 // head dim
 constexpr int kBlk = 128;               // queries per block, keys per tile
 constexpr int kBox = 128 * 128;         // one 64-column x 128-row bf16 box (16 KB)
 constexpr int kTile = 2 * kBox;         // one 128 x 128 bf16 tile (two boxes, 32 KB)
-constexpr int kSlots = 3;               // K / V ring slots
-constexpr int kWarpStg = 2 * 32 * 128;  // one warp's 32-row O staging (two 4 KB boxes)
-constexpr int kThreads = 320;
+#ifndef DEMON_ATTN_KV_SLOTS
+#define DEMON_ATTN_KV_SLOTS 3
+#endif
+constexpr int kSlots = DEMON_ATTN_KV_SLOTS;  // K / V ring slots
+constexpr int kQSlots = 3;                   // Q ring slots (one 128 x 128 tile of one head each)
+constexpr int kWarpStg = 2 * 32 * 128;       // one epilogue warp's 32-row O staging (two 4 KB boxes)
+constexpr int kThreads = 512;           // four warpgroups
 
-constexpr int offQ = 0;                                 // Q of both heads (64 KB)
-constexpr int offKV = offQ + 2 * kTile;                 // ring (96 KB)
-constexpr int offStg = offKV + kSlots * kTile;          // 8 warps x 8 KB
-constexpr int offBar = offStg + 8 * kWarpStg;           // mbarriers
-constexpr int kNumBars = 2 + 2 * kSlots + 2 * 4 + 1;
+// Registers per thread after the split (setmaxnreg): the launch gives 512 x 128; the two
+// softmax warpgroups take 176, the epilogue warpgroup 96, the TMA / MMA warpgroup 64:
+// 256 * 176 + 128 * 96 + 128 * 64 = 65,536 = 512 * 128.
+constexpr int kLaunchRegs = 128, kSoftmaxRegs = 176, kEpilogueRegs = 96, kIssueRegs = 64;
+static_assert(256 * kSoftmaxRegs + 128 * kEpilogueRegs + 128 * kIssueRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
+
+constexpr int offQ = 0;                                 // Q ring (96 KB)
+constexpr int offKV = offQ + kQSlots * kTile;           // K / V ring (96 KB)
+constexpr int offStg = offKV + kSlots * kTile;          // 4 epilogue warps x 8 KB
+constexpr int offL = offStg + 4 * kWarpStg;             // row sums: [2 heads][128 rows] fp32
+constexpr int offBar = offL + 2 * 128 * 4;              // mbarriers
+constexpr int kNumBars = 2 * kQSlots + 2 * kSlots + 2 * 7 + 1;
 constexpr int offMisc = offBar + kNumBars * 8;          // tmem holder, abort flag
 constexpr int kSmemUsed = offMisc + 16;
 constexpr int kSmem = kSmemUsed + 1024;                 // + alignment slack
@@ -84,7 +98,17 @@ struct Params {
 
 struct Unit {
   int b, hk, h0, qb, kt0, nt;  // sequence, kv head, first q head, query block, first key tile, tiles
+  int ktd;                     // key tile visited first (the band's diagonal tile; kt0 without a band)
 };
+
+// Key tile of step i of a unit: the diagonal tile first, then the others in order.  With a
+// band, rows whose first tile held only a few keys of their range would start from a poor
+// running maximum, and the next tile's would exceed it by more than 2^8 (an O rescale).
+__device__ __forceinline__ int key_tile(const Unit& w, int i) {
+  if (i == 0) return w.ktd;
+  const int k = w.kt0 + i - 1;
+  return k < w.ktd ? k : k + 1;
+}
 
 __device__ __forceinline__ Unit decode(const Params& p, int64_t u) {
   Unit w;
@@ -102,9 +126,11 @@ __device__ __forceinline__ Unit decode(const Params& p, int64_t u) {
     const int khi = min(p.L - 1, qlast + p.window);
     w.kt0 = klo / kBlk;
     w.nt = khi / kBlk - w.kt0 + 1;
+    w.ktd = min(max(q0 / kBlk, w.kt0), w.kt0 + w.nt - 1);
   } else {
     w.kt0 = 0;
     w.nt = p.n_kblk;
+    w.ktd = 0;
   }
   return w;
 }
@@ -136,7 +162,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // FMA pipe (exp2_poly2) instead of the MUFU unit, which alone would need as many cycles per
 // key tile as the tensor core: bit j set = pair j of the group.
 #ifndef DEMON_ATTN_POLY_PAIRS
-#define DEMON_ATTN_POLY_PAIRS 0x88
+#define DEMON_ATTN_POLY_PAIRS 0x00
 #endif
 constexpr unsigned kPolyPairs = DEMON_ATTN_POLY_PAIRS;
 
@@ -169,6 +195,15 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok && *abort == 0);
 }
 
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -177,15 +212,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + offBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;
-  uint64_t* kv_empty = bars + 2 + kSlots;
-  uint64_t* s_full = bars + 2 + 2 * kSlots;  // [2]
-  uint64_t* p_full = s_full + 2;             // [2]
-  uint64_t* o_full = s_full + 4;             // [2]
-  uint64_t* o_empty = s_full + 6;            // [2]
-  uint64_t* mma_done = s_full + 8;
+  // Q tiles go through their own ring in the order (unit 0, head 0), (unit 0, head 1),
+  // (unit 1, head 0), ...: Q tile 2 it + h of a CTA sits in slot (2 it + h) % 3, so the next
+  // unit's Q loads while the current unit still runs.
+  uint64_t* q_full = bars + 0;                         // [3] TMA -> MMA: Q tile loaded
+  uint64_t* q_empty = bars + kQSlots;                  // [3] MMA -> TMA: its last S computed
+  uint64_t* kv_full = bars + 2 * kQSlots;
+  uint64_t* kv_empty = bars + 2 * kQSlots + kSlots;
+  uint64_t* s_full = bars + 2 * kQSlots + 2 * kSlots;  // [2] MMA -> softmax: S_h computed
+  uint64_t* pa_full = s_full + 2;            // [2] softmax -> MMA: P_h of keys 0-63 in tensor memory
+  uint64_t* pb_full = s_full + 4;            // [2] softmax -> MMA: P_h of keys 64-127
+  uint64_t* o_full = s_full + 6;             // [2] MMA -> epilogue: the unit's last P V done
+  uint64_t* o_empty = s_full + 8;            // [2] epilogue -> MMA: O_h read out
+  uint64_t* l_full = s_full + 10;            // [2] softmax -> epilogue: row sums written
+  uint64_t* l_empty = s_full + 12;           // [2] epilogue -> softmax: row sums read
+  uint64_t* mma_done = s_full + 14;
+  const uint32_t lbuf = sbase + offL;        // [2][128] fp32
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + offMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + offMisc + 4);
 
@@ -193,29 +235,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint64_t t0 = globaltimer();
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int s = 0; s < kQSlots; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&s_full[h], 1);
-      mbar_init(&p_full[h], 4);   // one arrive per softmax warp
+      mbar_init(&pa_full[h], 4);  // one arrive per softmax warp
+      mbar_init(&pb_full[h], 4);
       mbar_init(&o_full[h], 1);
-      mbar_init(&o_empty[h], 4);  // one arrive per softmax warp
+      mbar_init(&o_empty[h], 4);  // one arrive per epilogue warp
+      mbar_init(&l_full[h], 4);   // one arrive per softmax warp
+      mbar_init(&l_empty[h], 4);  // one arrive per epilogue warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == 12 && lane == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
     prefetch_tmap(&tmO);
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(tmem_holder, kTmemCols);
     tmem_relinquish();
   }
@@ -224,143 +271,180 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int64_t stride = gridDim.x;
+  const int wg = warp >> 2;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
-    if (elect_one()) {
-      uint32_t g = 0, it = 0, nq = 0;  // K / V tiles issued, units started, Q pairs issued
-      bool ok = true;
-      for (int64_t u = blockIdx.x; ok && u < p.units; u += stride, ++it) {
-        const Unit w = decode(p, u);
-        if (!(ok = mbar_wait(q_empty, (it & 1u) ^ 1u, abort_flag, t0, p.status, 21))) break;
-        mbar_arrive_expect_tx(q_full, 2 * kTile);
-        for (int h = 0; h < 2; ++h)
+  if (wg == 3) {
+    setmaxnreg_dec<kIssueRegs>();
+    if (warp == 12) {
+      // ---------------------------------------------------------- TMA producer
+      if (elect_one()) {
+        uint32_t g = 0, it = 0, nq = 0;  // K / V tiles issued, units started, Q tiles issued
+        bool ok = true;
+        auto load_q = [&](const Unit& w, int h) {
+          const int s = (int)(nq % kQSlots);
+          if (!(ok = mbar_wait(&q_empty[s], ((nq / kQSlots) & 1u) ^ 1u, abort_flag, t0, p.status, 21))) return false;
+          mbar_arrive_expect_tx(&q_full[s], kTile);
           for (int half = 0; half < 2; ++half)
-            tma_load_3d(sbase + offQ + h * kTile + half * kBox, &tmQ, q_full, (w.h0 + h) * kD + half * 64,
+            tma_load_3d(sbase + offQ + s * kTile + half * kBox, &tmQ, &q_full[s], (w.h0 + h) * kD + half * 64,
                         w.qb * kBlk, w.b);
-        ++nq;
-        for (int i = 0; ok && i < w.nt; ++i) {
-          const int k0 = (w.kt0 + i) * kBlk;
-          for (int kv = 0; kv < 2; ++kv, ++g) {
-            const int s = (int)(g % kSlots);
-            if (!(ok = mbar_wait(&kv_empty[s], ((g / kSlots) & 1u) ^ 1u, abort_flag, t0, p.status, 22))) break;
-            mbar_arrive_expect_tx(&kv_full[s], kTile);
-            const CUtensorMap* m = kv ? &tmV : &tmK;
-            for (int half = 0; half < 2; ++half)
-              tma_load_3d(sbase + offKV + s * kTile + half * kBox, m, &kv_full[s], w.hk * kD + half * 64, k0, w.b);
+          ++nq;
+          return true;
+        };
+        // order per unit: Q of head 0, K / V of the first key tile, Q of head 1, the other tiles
+        // (the MMA issues the unit's first S_0 before the previous unit's last P_1 V)
+        for (int64_t u = blockIdx.x; ok && u < p.units; u += stride, ++it) {
+          const Unit w = decode(p, u);
+          if (!load_q(w, 0)) break;
+          for (int i = 0; ok && i < w.nt; ++i) {
+            const int k0 = key_tile(w, i) * kBlk;
+            for (int kv = 0; kv < 2; ++kv, ++g) {
+              const int s = (int)(g % kSlots);
+              if (!(ok = mbar_wait(&kv_empty[s], ((g / kSlots) & 1u) ^ 1u, abort_flag, t0, p.status, 22))) break;
+              mbar_arrive_expect_tx(&kv_full[s], kTile);
+              const CUtensorMap* m = kv ? &tmV : &tmK;
+              for (int half = 0; half < 2; ++half)
+                tma_load_3d(sbase + offKV + s * kTile + half * kBox, m, &kv_full[s], w.hk * kD + half * 64, k0,
+                            w.b);
+            }
+            if (ok && i == 0 && !load_q(w, 1)) break;
           }
         }
+        // drain: no copy may still be in flight when the CTA leaves (immediate on the normal path)
+        volatile int never = 0;
+        for (uint32_t i = g > (uint32_t)kSlots ? g - kSlots : 0; i < g; ++i)
+          mbar_wait(&kv_full[i % kSlots], (i / kSlots) & 1u, &never, globaltimer(), p.status, 23);
+        for (uint32_t i = nq > (uint32_t)kQSlots ? nq - kQSlots : 0; i < nq; ++i)
+          mbar_wait(&q_full[i % kQSlots], (i / kQSlots) & 1u, &never, globaltimer(), p.status, 24);
       }
-      // drain: no copy may still be in flight when the CTA leaves (immediate on the normal path)
-      volatile int never = 0;
-      for (uint32_t i = g > (uint32_t)kSlots ? g - kSlots : 0; i < g; ++i)
-        mbar_wait(&kv_full[i % kSlots], (i / kSlots) & 1u, &never, globaltimer(), p.status, 23);
-      if (nq) mbar_wait(q_full, (nq - 1) & 1u, &never, globaltimer(), p.status, 24);
-    }
-    __syncwarp();
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      const uint32_t idesc_qk = idesc_bf16(kBlk, kBlk);
-      const uint32_t idesc_pv = idesc_bf16(kBlk, kD) | (1u << 16);  // B (V) MN-major
-      uint32_t g = 0, it = 0, tiles = 0;  // K / V tiles consumed, units, key tiles (all units)
-      bool ok = true;
-      auto qk = [&](int h, uint32_t kslot) {
-        const uint32_t qa = sbase + offQ + h * kTile, kb = sbase + offKV + kslot * kTile;
+      __syncwarp();
+    } else if (warp == 13) {
+      // ---------------------------------------------------------- MMA issuer
+      if (elect_one()) {
+        const uint32_t idesc_qk = idesc_bf16(kBlk, kBlk);
+        const uint32_t idesc_pv = idesc_bf16(kBlk, kD) | (1u << 16);  // B (V) MN-major
+        uint32_t g = 0, it = 0, tiles = 0;  // K / V tiles consumed, units, key tiles (all units)
+        bool ok = true;
+        auto qk = [&](int h, uint32_t kslot) {
+          const uint32_t qa = sbase + offQ + ((2 * it + h) % kQSlots) * kTile, kb = sbase + offKV + kslot * kTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16(tmem + kColS + 128 * h, kmajor_desc(qa, kk), kmajor_desc(kb, kk), idesc_qk, kk > 0);
-        tc_commit(&s_full[h]);
-      };
-      auto pv = [&](int h, uint32_t vslot, bool acc) {
-        const uint32_t vb = sbase + offKV + vslot * kTile;
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16(tmem + kColS + 128 * h, kmajor_desc(qa, kk), kmajor_desc(kb, kk), idesc_qk, kk > 0);
+          tc_commit(&s_full[h]);
+        };
+        // O_h += P_h V over keys 64 half .. 64 half + 63 (acc = 0: the unit's first product)
+        auto pv = [&](int h, uint32_t vslot, int half, bool acc) {
+          const uint32_t vb = sbase + offKV + vslot * kTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(tmem + kColO + 128 * h, tmem + kColS + 128 * h + kColP + 8 * kk, mnmajor_desc(vb, kk),
-                      idesc_pv, (acc || kk > 0) ? 1u : 0u);
-      };
-      auto wait_kv = [&](uint32_t gi) {
-        ok = mbar_wait(&kv_full[gi % kSlots], (gi / kSlots) & 1u, abort_flag, t0, p.status, 31);
-        if (ok) tc_fence_after();
-        return ok;
-      };
-      auto wait_p = [&](int h, uint32_t t) {
-        ok = mbar_wait(&p_full[h], t & 1u, abort_flag, t0, p.status, 32 + h);
-        if (ok) tc_fence_after();
-        return ok;
-      };
-      auto wait_oe = [&](int h) {
-        ok = mbar_wait(&o_empty[h], (it & 1u) ^ 1u, abort_flag, t0, p.status, 34 + h);
-        if (ok) tc_fence_after();
-        return ok;
-      };
-      for (int64_t u = blockIdx.x; ok && u < p.units; u += stride, ++it) {
-        const Unit w = decode(p, u);
-        const int n = w.nt;
-        if (!(ok = mbar_wait(q_full, it & 1u, abort_flag, t0, p.status, 30))) break;
-        tc_fence_after();
-        // tile 0
-        uint32_t gk = g, gv = g + 1;
-        if (!wait_kv(gk)) break;
-        qk(0, gk % kSlots);
-        qk(1, gk % kSlots);
-        tc_commit(&kv_empty[gk % kSlots]);
-        if (n == 1) tc_commit(q_empty);
-        if (!wait_kv(gv) || !wait_oe(0) || !wait_p(0, tiles)) break;
-        pv(0, gv % kSlots, false);
-        uint32_t prev_v = gv;
-        g += 2;
-        for (int i = 1; i < n; ++i) {
-          gk = g;
-          gv = g + 1;
-          if (!wait_kv(gk)) break;
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = 4 * half + k4;
+            mma_bf16_ts(tmem + kColO + 128 * h, tmem + kColS + 128 * h + kColP + 8 * kk, mnmajor_desc(vb, kk),
+                        idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          }
+        };
+        auto wait_kv = [&](uint32_t gi) {
+          ok = mbar_wait(&kv_full[gi % kSlots], (gi / kSlots) & 1u, abort_flag, t0, p.status, 31);
+          if (ok) tc_fence_after();
+          return ok;
+        };
+        auto wait_p = [&](uint64_t* bar, int h, uint32_t t) {
+          ok = mbar_wait(&bar[h], t & 1u, abort_flag, t0, p.status, 32 + h);
+          if (ok) tc_fence_after();
+          return ok;
+        };
+        // both halves of P_h(t) into O_h: the first as soon as it is published
+        auto pv_tile = [&](int h, uint32_t vslot, uint32_t t, bool acc) {
+          if (!wait_p(pa_full, h, t)) return false;
+          pv(h, vslot, 0, acc);
+          if (!wait_p(pb_full, h, t)) return false;
+          pv(h, vslot, 1, true);
+          return true;
+        };
+        auto wait_oe = [&](int h) {
+          ok = mbar_wait(&o_empty[h], (it & 1u) ^ 1u, abort_flag, t0, p.status, 34 + h);
+          if (ok) tc_fence_after();
+          return ok;
+        };
+        auto wait_q = [&](int h) {
+          const uint32_t qi = 2 * it + h;
+          ok = mbar_wait(&q_full[qi % kQSlots], (qi / kQSlots) & 1u, abort_flag, t0, p.status, 30);
+          if (ok) tc_fence_after();
+          return ok;
+        };
+        auto free_q = [&](int h) { tc_commit(&q_empty[(2 * it + h) % kQSlots]); };
+        // The units form one stream of key tiles: the last P_1 V of a unit is issued after the
+        // next unit's first S_0 = Q K^T, as inside a unit, so head 0's softmax goes on without
+        // waiting for the unit boundary.
+        bool pend = false;  // the previous unit's last P_1 V is still to be issued
+        uint32_t pend_v = 0, pend_t = 0;
+        bool pend_acc = false;
+        auto flush = [&]() {
+          if (!pend) return true;
+          if (!pv_tile(1, pend_v % kSlots, pend_t, pend_acc)) return false;
+          tc_commit(&kv_empty[pend_v % kSlots]);
+          tc_commit(&o_full[1]);
+          pend = false;
+          return true;
+        };
+        for (int64_t u = blockIdx.x; ok && u < p.units; u += stride, ++it) {
+          const Unit w = decode(p, u);
+          const int n = w.nt;
+          // tile 0
+          uint32_t gk = g, gv = g + 1;
+          if (!wait_q(0) || !wait_kv(gk)) break;
           qk(0, gk % kSlots);
-          if (i == 1 && !wait_oe(1)) break;
-          if (!wait_p(1, tiles + i - 1)) break;
-          pv(1, prev_v % kSlots, i - 1 > 0);
-          tc_commit(&kv_empty[prev_v % kSlots]);
+          if (n == 1) free_q(0);
+          if (!flush() || !wait_q(1)) break;
           qk(1, gk % kSlots);
           tc_commit(&kv_empty[gk % kSlots]);
-          if (i == n - 1) tc_commit(q_empty);
-          if (!wait_kv(gv) || !wait_p(0, tiles + i)) break;
-          pv(0, gv % kSlots, true);
-          prev_v = gv;
+          if (n == 1) free_q(1);
+          if (!wait_kv(gv) || !wait_oe(0) || !pv_tile(0, gv % kSlots, tiles, false)) break;
+          uint32_t prev_v = gv;
           g += 2;
+          for (int i = 1; i < n; ++i) {
+            gk = g;
+            gv = g + 1;
+            if (!wait_kv(gk)) break;
+            qk(0, gk % kSlots);
+            if (i == n - 1) free_q(0);
+            if (i == 1 && !wait_oe(1)) break;
+            if (!pv_tile(1, prev_v % kSlots, tiles + i - 1, i - 1 > 0)) break;
+            tc_commit(&kv_empty[prev_v % kSlots]);
+            qk(1, gk % kSlots);
+            tc_commit(&kv_empty[gk % kSlots]);
+            if (i == n - 1) free_q(1);
+            if (!wait_kv(gv) || !pv_tile(0, gv % kSlots, tiles + i, true)) break;
+            prev_v = gv;
+            g += 2;
+          }
+          if (!ok) break;
+          tc_commit(&o_full[0]);
+          if (n == 1 && !wait_oe(1)) break;  // this unit's only P_1 V overwrites O_1
+          pend = true;
+          pend_v = prev_v;
+          pend_t = tiles + n - 1;
+          pend_acc = n > 1;
+          tiles += n;
         }
-        if (!ok) break;
-        tc_commit(&o_full[0]);
-        if (n == 1 && !wait_oe(1)) break;
-        if (!wait_p(1, tiles + n - 1)) break;
-        pv(1, prev_v % kSlots, n > 1);
-        tc_commit(&kv_empty[prev_v % kSlots]);
-        tc_commit(&o_full[1]);
-        tiles += n;
+        if (ok) flush();  // the last unit's last P_1 V
+        tc_commit(mma_done);  // every MMA has completed before the tensor memory is freed
       }
-      if (!ok) {  // wake the softmax warps on the abort path
-        for (int h = 0; h < 2; ++h) {
-          tc_commit(&s_full[h]);
-          tc_commit(&o_full[h]);
-        }
+      __syncwarp();
+      {
+        volatile int never = 0;
+        mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 39);
       }
-      tc_commit(mma_done);  // every MMA has completed before the tensor memory is freed
+      __syncwarp();
     }
-    __syncwarp();
-    {
-      volatile int never = 0;
-      mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 39);
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int h = warp >> 2;          // q head of the pair
+  } else if (wg < 2) {
+    setmaxnreg_inc<kSoftmaxRegs>();
+    // ------------------------------------------------------------ softmax
+    const int h = wg;                 // q head of the pair
     const int quad = warp & 3;        // tensor-memory lane quadrant of this warp
     const int r = quad * 32 + lane;   // query row within the block
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_addr + kColS + 128 * h;
     const uint32_t o_addr = tmem + lane_addr + kColO + 128 * h;
-    const uint32_t stg = sbase + offStg + warp * kWarpStg;
     uint32_t t = 0, it = 0;
-    bool stored = false;
     for (int64_t u = blockIdx.x; u < p.units; u += stride, ++it) {
       const Unit w = decode(p, u);
       const int q0 = w.qb * kBlk, qi = q0 + r;
@@ -376,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
         tmem_ld_wait();
         float* s = reinterpret_cast<float*>(sr);
-        const int k0 = (w.kt0 + i) * kBlk;
+        const int k0 = key_tile(w, i) * kBlk;
         const bool band_full = p.window < 0 || (q0 + kBlk - 1 - k0 <= p.window && k0 + kBlk - 1 - q0 <= p.window);
         if (k0 + kBlk > p.L || !band_full) {  // mask keys past the end and outside the band
           int lo = 0, hi = min(kBlk - 1, p.L - 1 - k0);
@@ -411,23 +495,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= factor;
           m = mt;
         }
-        if (__any_sync(0xffffffffu, rescale)) {  // O_h is idle here (see the MMA order above)
-#pragma unroll 1
-          for (int c = 0; c < 16; ++c) {  // 8 columns at a time: the 128 scores stay in registers
-            uint32_t o[8];
-            tmem_ld_32x32b_x8(o_addr + 8 * c, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
-            tmem_st_32x32b_x8(o_addr + 8 * c, o);
-          }
-        }
         const float mo = (m == -INFINITY) ? 0.0f : m;
         const float2 sc = make_float2(p.scale_log2, p.scale_log2), nm = make_float2(-mo, -mo);
         float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
                          make_float2(0.0f, 0.0f)};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
+          if (c == 2) {  // keys 0-63 published: their P V starts while keys 64-127 are computed
+            if (__any_sync(0xffffffffu, rescale)) {
+              // O_h *= factor before this tile's first P V (O_h is idle: see the MMA order
+              // above); here half of the scores' registers are free for 32-column chunks
+#pragma unroll
+              for (int oc = 0; oc < 4; ++oc) {
+                uint32_t o[32];
+                tmem_ld_32x32b_x32(o_addr + 32 * oc, o);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
+                tmem_st_32x32b_x32(o_addr + 32 * oc, o);
+              }
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pa_full[h]);
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -443,42 +535,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[h]);
+        if (lane == 0) mbar_arrive(&pb_full[h]);
       }
       if (!ok) break;
-      // ---- epilogue: O_h rows of this warp -> bf16, 1 / rowsum, TMA store
-      if (!warp_wait(&o_full[h], it & 1u, abort_flag, t0, p.status, 42 + h)) break;
-      tc_fence_after();
-      uint32_t o[128];
-      tmem_ld_32x32b_x32(o_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(o + 0));
-      tmem_ld_32x32b_x32(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
-      tmem_ld_32x32b_x32(o_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(o + 64));
-      tmem_ld_32x32b_x32(o_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(o + 96));
-      tmem_ld_wait();
-      tc_fence_before();
+      // hand the row sums to the epilogue warps and go on with the next unit
+      if (!warp_wait(&l_empty[h], (it & 1u) ^ 1u, abort_flag, t0, p.status, 44 + h)) break;
+      st_shared_f32(lbuf + 4 * (h * 128 + r), l);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[h]);
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      if (stored) {  // the previous unit's store has finished reading the staging boxes
-        if (lane == 0) bulk_wait_read<0>();
+      if (lane == 0) mbar_arrive(&l_full[h]);
+    }
+  } else {
+    setmaxnreg_dec<kEpilogueRegs>();
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    const uint32_t stg = sbase + offStg + quad * kWarpStg;
+    uint32_t it = 0;
+    bool stored = false;
+    for (int64_t u = blockIdx.x; u < p.units; u += stride, ++it) {
+      const Unit w = decode(p, u);
+      const int q0 = w.qb * kBlk;
+      bool ok = true;
+      for (int h = 0; h < 2; ++h) {
+        if (!(ok = warp_wait(&l_full[h], it & 1u, abort_flag, t0, p.status, 46 + h))) break;
+        float lr;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(lr) : "r"(lbuf + 4 * (h * 128 + r)) : "memory");
         __syncwarp();
-      }
+        if (lane == 0) mbar_arrive(&l_empty[h]);
+        const float inv = lr > 0.0f ? 1.0f / lr : 0.0f;
+        if (!(ok = warp_wait(&o_full[h], it & 1u, abort_flag, t0, p.status, 42 + h))) break;
+        tc_fence_after();
+        if (stored) {  // the previous store has finished reading the staging boxes
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+        const uint32_t o_addr = tmem + lane_addr + kColO + 128 * h;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {  // 16-byte chunk j of the row: columns 8 j .. 8 j + 7
-        const float* f = reinterpret_cast<const float*>(o + 8 * j);
-        const uint32_t a = stg + (j >> 3) * 4096 + lane * 128 + (((j & 7) ^ (lane & 7)) << 4);
-        st_shared_v4(a, pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
-                     pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
+        for (int c = 0; c < 4; ++c) {  // 32 columns at a time
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_addr + 32 * c, o);
+          tmem_ld_wait();
+          if (c == 3) {  // O_h fully read: the next unit's P V may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_empty[h]);
+          }
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {  // 16-byte chunk j = 4 c + jj of the row: columns 8 j .. 8 j + 7
+            const int j = 4 * c + jj;
+            const float* f = reinterpret_cast<const float*>(o + 8 * jj);
+            const uint32_t a = stg + (j >> 3) * 4096 + lane * 128 + (((j & 7) ^ (lane & 7)) << 4);
+            st_shared_v4(a, pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
+                         pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && q0 + quad * 32 < p.S) {
+          for (int half = 0; half < 2; ++half)
+            tma_store_3d(&tmO, stg + half * 4096, (w.h0 + h) * kD + half * 64, q0 + quad * 32, w.b);
+          bulk_commit();
+          stored = true;
+        }
+        stored = __shfl_sync(0xffffffffu, stored, 0);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && q0 + quad * 32 < p.S) {
-        for (int half = 0; half < 2; ++half)
-          tma_store_3d(&tmO, stg + half * 4096, (w.h0 + h) * kD + half * 64, q0 + quad * 32, w.b);
-        bulk_commit();
-        stored = true;
-      }
-      stored = __shfl_sync(0xffffffffu, stored, 0);
+      if (!ok) break;
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -487,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 9) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 13) tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace attn
@@ -561,6 +683,15 @@ extern "C" int demon_attention(const DemonAttnArgs* a, void* stream) {
   p.units = (int64_t)a->B * a->Hk * p.pairs * p.n_qblk;
   p.status = status_word();
   if (device_pending(g_attn_attr)) {
+    // the warpgroups' register split adds up to exactly the launch's registers; with any
+    // other per-thread count at launch the softmax warps' setmaxnreg.inc would never return
+    cudaFuncAttributes fa;
+    DEMON_CUDA(cudaFuncGetAttributes(&fa, attn::attention_kernel));
+    if (fa.numRegs != attn::kLaunchRegs) {
+      set_error("attention: kernel built with %d registers per thread, the register split needs %d", fa.numRegs,
+                attn::kLaunchRegs);
+      return DEMON_ERR_CUDA;
+    }
     DEMON_CUDA(cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmem));
     mark_device_done(g_attn_attr);
   }

@@ -230,6 +230,11 @@ __device__ __forceinline__ void st_global_v4(void* p, uint4 v) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
+// Streaming store (.cs: likely read at most once, evicted first).
+__device__ __forceinline__ void st_global_cs_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
 // 64 contiguous bytes (32 bf16) of one row, as four 16-byte loads.
 __device__ __forceinline__ void ld_global_row64(const void* p, uint4 (&r)[4]) {
 #pragma unroll

@@ -24,9 +24,10 @@ Data path of one layer (M = B * S rows of the residual stream ``h``):
 Every DiT linear that the reference's low-precision export quantises (all but
 ``time_embed*``, acestep/engine/trt/fp8_onnx.py:101-104) runs in NVFP4; proj_in,
 proj_out and the timestep MLPs stay bf16 on the tensor cores (``demon_bf16_linear``).
-Every kernel here computes a row from that row alone, and attention runs cuDNN fused attention
-with a fixed (unsplit) KV loop, so a sequence's output does not depend on the batch it
-is computed in: the streaming ring and a single request give identical bits.
+Every kernel here computes a row from that row alone, and the attention kernel walks each
+sequence's key tiles in a fixed order (no split over the keys), so a sequence's output does
+not depend on the batch it is computed in: the streaming ring and a single request give
+identical bits.
 Hot LoRA on a linear switches that projection to its own GEMM (LoRA ranks of fused
 projections do not share one down-projection).
 """
@@ -37,80 +38,10 @@ from dataclasses import dataclass
 
 import torch
 from torch import nn
-from torch.nn.attention import SDPBackend, sdpa_kernel
-
 from . import nvfp4 as Q
+from .attention import attention as _attention_kernel
 from .nvfp4 import NVFP4Linear
 from .rowops import adanorm_quantize, head_norm_rope, silu_mul_quantize
-
-try:  # cuDNN frontend (library): fused attention with a diagonal band for the sliding window
-    import cudnn as _cudnn
-    _cudnn_error = None
-except Exception as _e:  # pragma: no cover - import depends on the image
-    _cudnn = None
-    _cudnn_error = _e
-
-
-class _BandAttention:
-    """Bidirectional sliding-window attention ``|i - j| <= window`` (the reference's 4-D
-    sliding mask, turbo.py:63-137) as one cuDNN fused-attention graph with a diagonal band
-    (left bound window + 1, right bound window), GQA native, reading q / k / v through their
-    strides.  One graph per (shape, strides, window), built on first use and replayed (also
-    inside CUDA graph capture); its workspace is kept with it."""
-
-    def __init__(self):
-        self._handles: dict = {}
-        self._graphs: dict = {}
-
-    def _handle(self, dev):
-        h = self._handles.get(dev.index)
-        if h is None:
-            with torch.cuda.device(dev):
-                h = self._handles[dev.index] = _cudnn.create_handle()
-        return h
-
-    def _build(self, handle, B, S, L, Hq, Hk, D, window, strides, dev):
-        c = _cudnn
-        g = c.pygraph(io_data_type=c.data_type.BFLOAT16, intermediate_data_type=c.data_type.FLOAT,
-                      compute_data_type=c.data_type.FLOAT, handle=handle)
-        qs, ks, vs, os_ = strides
-        q = g.tensor(name="q", dim=[B, Hq, S, D], stride=list(qs), data_type=c.data_type.BFLOAT16)
-        k = g.tensor(name="k", dim=[B, Hk, L, D], stride=list(ks), data_type=c.data_type.BFLOAT16)
-        v = g.tensor(name="v", dim=[B, Hk, L, D], stride=list(vs), data_type=c.data_type.BFLOAT16)
-        o, _ = g.sdpa(q=q, k=k, v=v, is_inference=True, attn_scale=D ** -0.5,
-                      diagonal_band_left_bound=window + 1, diagonal_band_right_bound=window)
-        o.set_output(True).set_dim([B, Hq, S, D]).set_stride(list(os_)).set_data_type(c.data_type.BFLOAT16)
-        g.validate()
-        g.build_operation_graph()
-        g.create_execution_plans([c.heur_mode.A, c.heur_mode.FALLBACK])
-        g.check_support()
-        g.build_plans()
-        ws = torch.empty(max(1, g.get_workspace_size()), dtype=torch.uint8, device=dev)
-        return g, (q, k, v, o), ws
-
-    def __call__(self, q, k, v, window: int):
-        if _cudnn is None:
-            raise RuntimeError(f"the cuDNN frontend is required for the DiT sliding-window attention: "
-                               f"{_cudnn_error!r}")
-        B, S, Hq, D = q.shape
-        L, Hk = k.shape[1], k.shape[2]
-        dev = q.device
-        out = torch.empty(B, S, Hq, D, dtype=torch.bfloat16, device=dev)
-        qv, kv, vv, ov = (t.transpose(1, 2) for t in (q, k, v, out))
-        strides = tuple(tuple(t.stride()) for t in (qv, kv, vv, ov))
-        key = (dev.index, B, S, L, Hq, Hk, D, window, strides)
-        handle = self._handle(dev)
-        ent = self._graphs.get(key)
-        if ent is None:
-            ent = self._graphs[key] = self._build(handle, B, S, L, Hq, Hk, D, window, strides, dev)
-        g, (tq, tk, tv, to), ws = ent
-        _cudnn.set_stream(handle=handle, stream=torch.cuda.current_stream(dev).cuda_stream)
-        g.execute({tq: qv, tk: kv, tv: vv, to: ov}, ws, handle=handle)
-        return out
-
-
-_band_attention = _BandAttention()
-
 
 @dataclass
 class DiTConfig:
@@ -149,20 +80,17 @@ class RMSNorm(nn.Module):
 
 
 def _attention(q, k, v, window: int | None):
-    """softmax(q k^T / sqrt(128)) v, GQA, optional bidirectional band |i - j| <= window.
-    q [B, S, Hq, 128], k / v [B, L, Hk, 128] (strided views are fine); returns [B, S, Hq, 128].
+    """softmax(q k^T / sqrt(128)) v over the GQA-shared heads, optional bidirectional band
+    |i - j| <= window (the attention interface of AceStepAttention.forward, turbo.py:358-372,
+    and its sliding-window mask, :110-112).  q [B, S, Hq, 128], k / v [B, L, Hk, 128]
+    (strided views of the fused projection outputs are fine); returns [B, S, Hq, 128].
 
-    cuDNN fused attention (library), which computes each (sequence, head, query tile) from that
-    sequence alone (no split over the keys), so results do not depend on the batch: full
-    attention (global self-attention layers, cross-attention) through PyTorch SDPA, the
-    sliding-window layers as a diagonal-band graph of the cuDNN frontend.
+    The sm_100a attention kernel (demon_attention): each (sequence, q-head pair, 128-query
+    block) is computed from that sequence alone, over its key tiles in a fixed order, so
+    results do not depend on the batch.
     """
-    if window is None:
-        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
-            o = torch.nn.functional.scaled_dot_product_attention(
-                q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), enable_gqa=True)
-        return o.transpose(1, 2)
-    return _band_attention(q, k, v, window)
+    return _attention_kernel(q, k, v, window)
+
 
 class TimestepEmbedding(nn.Module):
     """turbo.py:207-261; the three linears stay bf16 (the reference never quantises time_embed)."""

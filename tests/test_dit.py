@@ -113,8 +113,8 @@ def test_dit_nvfp4_forward_matches_reference_fake_quant(cuda):
 
 @pytest.mark.gpu
 def test_attention_batch_invariant_at_dit_shapes(cuda):
-    """The DiT attention (cuDNN full / cross / diagonal-band window) computes a sequence from
-    that sequence alone at the DiT's shapes (750 tokens, GQA 16/8, text 256)."""
+    """The DiT attention (the sm_100a kernel: global, cross and the diagonal band) computes a
+    sequence from that sequence alone at the DiT's shapes (750 tokens, GQA 16/8, text 256)."""
     from demon_b200.dit import _attention
     g = torch.Generator(device=cuda).manual_seed(0)
     B, S, L = 6, 750, 256
