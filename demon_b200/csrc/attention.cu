@@ -11,25 +11,28 @@
 // Work unit: one (sequence, kv head, pair of q heads of that kv head, 128-query block).  Both
 // q heads read the same K / V tiles, so each 128-key K / V tile is loaded into shared memory
 // once per unit and used by four MMAs (S = Q K^T and O += P V for each head).  Persistent
-// CTAs (one per SM) walk the units in a static round-robin.
+// CTAs (one per SM) walk the units in a static round-robin; a band unit visits its diagonal
+// key tile first (rows then start from a running maximum over 128 keys).
 //
-// Warp roles (320 threads):
-//   warps 0-3  softmax + epilogue of q head 0 of the unit (one query row per thread),
-//   warps 4-7  the same for q head 1,
-//   warp  8    TMA loads (Q pair, then K_i, V_i for each key tile into a 3-slot ring),
-//   warp  9    MMA issue (one thread) and tensor-memory allocation.
+// Warp roles (512 threads, four warpgroups; setmaxnreg moves registers from the issuing
+// warpgroup to the softmax warpgroups):
+//   warpgroup 0 / 1  softmax of q head 0 / 1 of the unit, one query row per thread,
+//   warpgroup 2      epilogue: O_h / rowsum -> bf16 -> swizzled shared memory -> TMA store,
+//   warp 12          TMA loads: Q tiles into a 3-slot ring, K / V tiles into a 3-slot ring,
+//   warp 13          MMA issue (one thread) and tensor-memory allocation.
 // Tensor memory (512 columns): S_h at 128 h, O_h at 256 + 128 h (fp32, row = lane); P_h, the
 // bf16 probabilities, overwrite the upper half of S_h (columns 128 h + 64 ..) and feed the
 // P V MMA straight from tensor memory.  The MMAs of one thread run in issue order, which is
 // what lets the next S_h = Q K^T overwrite P_h: it is issued after the P V that reads it.
 //
-// MMA order per unit with n key tiles (the S of one head is computed while the other head's
-// softmax runs):
-//   QK0(0) QK1(0) PV0(0) | for i >= 1: QK0(i) PV1(i-1) QK1(i) PV0(i) | PV1(n-1)
-// Each PV is issued in two halves of 64 keys: the softmax publishes the probabilities of keys
-// 0-63 first, and their product runs while it computes those of keys 64-127.
-// The commit that signals S_h(i) therefore also covers PV_h(i-1): when a softmax warp sees
-// S_h(i), no MMA touches O_h until it publishes P_h(i), so it may rescale O_h in place.
+// MMA order, the units of a CTA forming one stream of key tiles (i = tile of the unit):
+//   QK0(i) PV1(i-1) QK1(i) PV0(i)
+// with PV1 of a unit's last tile issued after the next unit's QK0(0), so the softmax of
+// head 0 runs on into the next unit while head 1 finishes.  Each PV is issued in two halves
+// of 64 keys: the softmax publishes the probabilities of keys 0-63 first, and their product
+// runs while it computes those of keys 64-127.  The commit that signals S_h(i) also covers
+// PV_h(i-1): when a softmax warp sees S_h(i), no MMA touches O_h until it publishes P_h(i),
+// so it may rescale O_h in place.
 //
 // Softmax (per row, log2 domain): t = s * scale * log2(e).  The running offset m is only
 // raised when a tile's row maximum exceeds it by more than 8 (then O_h and the row sum are
@@ -37,10 +40,10 @@
 // Numerator and denominator use the same offset, so the result is the exact softmax up to
 // rounding (the lazy rescaling of FlashAttention-4, Dao et al. 2025).
 //
-// Epilogue: after the unit's last P V, each softmax warp reads its 32 rows of O_h from
-// tensor memory, hands the columns back to the MMA warp, scales by 1 / rowsum, and stores
-// the bf16 rows through a swizzled shared-memory box with its own TMA stores (rows past the
-// sequence end are clipped by the tensor map).
+// Epilogue: after a unit's last P V of head h, the epilogue warps read O_h from tensor memory
+// (and hand its columns back to the MMA warp), scale each row by 1 / rowsum (handed over by
+// the softmax warps through shared memory) and store the bf16 rows with per-warp TMA stores
+// (rows past the sequence end are clipped by the tensor map).
 //
 // Every wait is a bounded mbarrier wait; on expiry the kernel records DEMON_DEV_TIMEOUT in
 // the status word, every role leaves its loop, outstanding copies and MMAs are waited for
@@ -58,10 +61,7 @@ constexpr int kD = 128;                 // head dim
 constexpr int kBlk = 128;               // queries per block, keys per tile
 constexpr int kBox = 128 * 128;         // one 64-column x 128-row bf16 box (16 KB)
 constexpr int kTile = 2 * kBox;         // one 128 x 128 bf16 tile (two boxes, 32 KB)
-#ifndef DEMON_ATTN_KV_SLOTS
-#define DEMON_ATTN_KV_SLOTS 3
-#endif
-constexpr int kSlots = DEMON_ATTN_KV_SLOTS;  // K / V ring slots
+constexpr int kSlots = 3;                    // K / V ring slots
 constexpr int kQSlots = 3;                   // Q ring slots (one 128 x 128 tile of one head each)
 constexpr int kWarpStg = 2 * 32 * 128;       // one epilogue warp's 32-row O staging (two 4 KB boxes)
 constexpr int kThreads = 512;           // four warpgroups
@@ -156,36 +156,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// Pairs of probabilities (within each group of eight pairs of a row) whose 2^x runs on the
-// FMA pipe (exp2_poly2) instead of the MUFU unit, which alone would need as many cycles per
-// key tile as the tensor core: bit j set = pair j of the group.
-#ifndef DEMON_ATTN_POLY_PAIRS
-#define DEMON_ATTN_POLY_PAIRS 0x00
-#endif
-constexpr unsigned kPolyPairs = DEMON_ATTN_POLY_PAIRS;
-
-// 2^x for a pair, x <= 128, on the FMA pipe: range reduction x = j + r with j = rint(x)
-// (Cody-Waite: adding 1.5 * 2^23 rounds to an integer in the low mantissa bits) and
-// r in [-1/2, 1/2]; 2^r by a degree-3 polynomial whose coefficients are a relative-error
-// minimax fit (Lawson's iteratively reweighted least squares, 4001 Chebyshev nodes; max
-// relative error 7.5e-5 in fp32, below the bf16 rounding the probabilities get next); 2^j
-// is added to the exponent field.  x is clamped at -126, where 2^x no longer matters next
-// to the row's largest term (>= 1).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  const float magic = 12582912.0f;  // 1.5 * 2^23
-  x = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
-  const float2 t = add_f2(x, make_float2(magic, magic));
-  const float2 j = add_f2(t, make_float2(-magic, -magic));
-  const float2 r = fma_f2(j, make_float2(-1.0f, -1.0f), x);
-  float2 q = fma_f2(make_float2(0.0551716685f, 0.0551716685f), r, make_float2(0.2426111400f, 0.2426111400f));
-  q = fma_f2(q, r, make_float2(0.6932609677f, 0.6932609677f));
-  q = fma_f2(q, r, make_float2(0.9999280572f, 0.9999280572f));
-  // bits(t) = bits(1.5 * 2^23) + j, whose low 9 bits are those of j; shifted by 23 the
-  // constant part vanishes modulo 2^32, leaving j << 23
-  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
 // A warp-uniform bounded wait: every lane waits, and the warp proceeds only if all did.
@@ -524,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float2 x = fma_f2(make_float2(s[32 * c + 2 * j], s[32 * c + 2 * j + 1]), sc, nm);
-            const float2 e = ((kPolyPairs >> (j & 7)) & 1) ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+            const float2 e = make_float2(ex2(x.x), ex2(x.y));
             acc[j & 3] = add_f2(acc[j & 3], e);
             pk[j] = pack_bf16x2(e.x, e.y);
           }
