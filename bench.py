@@ -1373,7 +1373,10 @@ def run_kernel_workload(args):
     ``gemm``: NVFP4 linears of shapes ``--shape M,N,K[:M,N,K...]`` (inputs quantised and weights
     packed before timing), launched shape by shape in each warm-up and timed pass;
     ``rows``: the 64-slot ODE step, the AdaLN-RMSNorm quantiser on [12000, 2048], SiLU*up on
-    [12000, 12288] and the activation quantiser on [12000, 2048].  Prints per-launch times."""
+    [12000, 12288] and the activation quantiser on [12000, 2048];
+    ``attention``: the DiT's band (window 128), global and cross attention over ``--seqs``
+    sequences of 750 tokens (GQA 16/8 x 128, text 256), with ``--vs-cudnn`` also the cuDNN
+    kernels on the same inputs.  Prints per-launch times."""
     import torch
     from demon_b200 import _build, _native as nat, nvfp4
     _build.build()
@@ -1396,6 +1399,35 @@ def run_kernel_workload(args):
                 launches.append((f"cublaslt {M}x{N}x{K}", 2.0 * M * N * K,
                                  lambda fa=fa, fb=fb, sa=sa, sb=sb: torch._scaled_mm(
                                      fa, fb, sa, sb, out_dtype=torch.bfloat16)))
+    elif args.workload == "attention":
+        from demon_b200.attention import attention
+        B, S, L, hq, hk, D = args.seqs, 750, L5, 16, 8, 128
+        qkv = torch.randn(B * S, (hq + 2 * hk) * D, generator=g, device=dev).to(torch.bfloat16)
+        ld = qkv.stride(0)
+        q = qkv.as_strided((B, S, hq, D), (S * ld, ld, D, 1))
+        k = qkv.as_strided((B, S, hk, D), (S * ld, ld, D, 1), hq * D)
+        v = qkv.as_strided((B, S, hk, D), (S * ld, ld, D, 1), (hq + hk) * D)
+        kvx = torch.randn(B * L, 2 * hk * D, generator=g, device=dev).to(torch.bfloat16)
+        lk = kvx.stride(0)
+        ck = kvx.as_strided((B, L, hk, D), (L * lk, lk, D, 1))
+        cv = kvx.as_strided((B, L, hk, D), (L * lk, lk, D, 1), hk * D)
+        qc = torch.randn(B, S, hq, D, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty(B, S, hq, D, dtype=torch.bfloat16, device=dev)
+        n_band = sum(min(i + 128, S - 1) - max(i - 128, 0) + 1 for i in range(S))
+        launches += [("attention band", 4.0 * B * hq * n_band * D, lambda: attention(q, k, v, 128, out=out)),
+                     ("attention global", 4.0 * B * hq * S * S * D, lambda: attention(q, k, v, out=out)),
+                     ("attention cross", 4.0 * B * hq * S * L * D, lambda: attention(qc, ck, cv, out=out))]
+        if args.vs_cudnn:
+            from torch.nn.attention import SDPBackend, sdpa_kernel
+            band = _CudnnBand()
+
+            def sdpa(qq, kk, vv):
+                with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                    return torch.nn.functional.scaled_dot_product_attention(
+                        qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2), enable_gqa=True)
+            launches += [("cudnn band", 4.0 * B * hq * n_band * D, lambda: band(q, k, v, 128)),
+                         ("cudnn global", 4.0 * B * hq * S * S * D, lambda: sdpa(q, k, v)),
+                         ("cudnn cross", 4.0 * B * hq * S * L * D, lambda: sdpa(qc, ck, cv))]
     else:
         from demon_b200.rowops import adanorm_quantize, silu_mul_quantize
         tick, nbytes, gain = ode_workload(dev, nslots=64, T=1500, seed=0)
@@ -1427,8 +1459,9 @@ def run_kernel_workload(args):
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.steps
-        unit = "TFLOP/s" if args.workload == "gemm" else "GB/s"
-        res[name] = {"us": us, unit: work / (us * 1e-6) / (1e12 if args.workload == "gemm" else 1e9)}
+        flops = args.workload in ("gemm", "attention")
+        unit = "TFLOP/s" if flops else "GB/s"
+        res[name] = {"us": us, unit: work / (us * 1e-6) / (1e12 if flops else 1e9)}
     print(json.dumps({"workload": args.workload, "shape": args.shape, "steps": args.steps, "kernels": res,
                       "device_status": list(nat.device_status())}), flush=True)
 
@@ -1439,7 +1472,10 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows"])
+    ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows", "attention"])
+    ap.add_argument("--seqs", type=int, default=128, help="sequences of 750 tokens for --workload attention")
+    ap.add_argument("--vs-cudnn", action="store_true",
+                    help="with --workload attention: also time the cuDNN attention kernels on the same inputs")
     ap.add_argument("--vs-cublaslt", action="store_true",
                     help="with --workload gemm: also time cuBLASLt's NVFP4 GEMM (torch._scaled_mm) on the same operands")
     ap.add_argument("--shape", default="12000,6144,2048", help="M,N,K[:M,N,K...] of --workload gemm")
@@ -1456,7 +1492,7 @@ def main():
     if args.impl == "reference":
         (run_reference_stream if args.workload == "stream" else run_reference)(args)
         return
-    if args.workload in ("gemm", "rows"):
+    if args.workload in ("gemm", "rows", "attention"):
         run_kernel_workload(args)
         return
     (run_stream if args.workload == "stream" else run_linear)(args)
