@@ -1372,8 +1372,9 @@ def run_kernel_workload(args):
     """Kernel-level workloads (one GPU), also the commands the ncu summaries under profiles/ use:
     ``gemm``: NVFP4 linears of shapes ``--shape M,N,K[:M,N,K...]`` (inputs quantised and weights
     packed before timing), launched shape by shape in each warm-up and timed pass;
-    ``rows``: the 64-slot ODE step, the AdaLN-RMSNorm quantiser on [12000, 2048], SiLU*up on
-    [12000, 12288] and the activation quantiser on [12000, 2048];
+    ``rows``: the 64-slot ODE step, the AdaLN-RMSNorm quantiser on [M, 2048], SiLU*up on
+    [M, 12288] and the activation quantiser on [M, 2048] (M = ``--shape`` when it is one
+    number, else 12000; the tick's is 96000);
     ``attention``: the DiT's band (window 128), global and cross attention over ``--seqs``
     sequences of 750 tokens (GQA 16/8 x 128, text 256), with ``--vs-cudnn`` also the cuDNN
     kernels on the same inputs.  Prints per-launch times."""
@@ -1433,11 +1434,12 @@ def run_kernel_workload(args):
         tick, nbytes, gain = ode_workload(dev, nslots=64, T=1500, seed=0)
         b, nb = tick._stage()
         tick._dev[b][:nb].copy_(tick._host[b][:nb])
-        M, D, F = 12000, 2048, 6144
+        M, D, F = (int(args.shape) if args.shape.isdigit() else 12000), 2048, 6144
         h = torch.randn(M, D, generator=g, device=dev).to(torch.bfloat16)
         w = torch.ones(D, device=dev, dtype=torch.bfloat16)
-        sc = torch.ones(16, D, device=dev, dtype=torch.bfloat16)
-        sh = torch.zeros(16, D, device=dev, dtype=torch.bfloat16)
+        nmod = (M + 749) // 750  # one modulation row per 750-token sequence
+        sc = torch.ones(nmod, D, device=dev, dtype=torch.bfloat16)
+        sh = torch.zeros(nmod, D, device=dev, dtype=torch.bfloat16)
         gu = torch.randn(M, 2 * F, generator=g, device=dev).to(torch.bfloat16)
         launches += [
             ("ode_step", nbytes, lambda: nat.check(nat.load().demon_ode_step(

@@ -22,6 +22,15 @@ namespace demon {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// sum / D rounded to fp32; for a power-of-two D the product with 1 / D is the same exact
+// quotient rounded once (scaling by a power of two), without the division's instruction
+// sequence.
+template <int D>
+__device__ __forceinline__ float mean_of_sum(float sum) {
+  if constexpr ((D & (D - 1)) == 0) return __fmul_rn(sum, 1.0f / (float)D);
+  return __fdiv_rn(sum, (float)D);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) { return pack_bf16x2(lo, hi); }
 
 struct NormArgs {
@@ -109,13 +118,14 @@ __global__ void __launch_bounds__(256) adanorm_quant_kernel(const NormArgs a) {
 #pragma unroll
   for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
   ss = row_reduce<G::W, false>(ss, red, warp, lane);
-  const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
-  float am = 0.0f;
+  const float rinv = __frsqrt_rn(__fadd_rn(mean_of_sum<D>(ss), a.eps));
+  uint32_t vmax[2 * G::NB];
 #pragma unroll
   for (int j = 0; j < 2 * G::NB; ++j) {
     xv[j] = norm8<MUL, ADD>(xv[j], wv[j], sv[j], hv[j], rinv);
-    am = fmaxf(am, absmax8_fast(xv[j]));
+    vmax[j] = absmax_bits8(xv[j]);
   }
+  float am = lane_absmax(xv, vmax);
   if (a.y && live) {
     uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
 #pragma unroll
@@ -138,10 +148,20 @@ __global__ void __launch_bounds__(256) adanorm_quant_kernel(const NormArgs a) {
   if (wr == 0 && lane == 0) a.gs[m] = g;
   const float denom = __fmul_rn(6.0f, g);
   uint8_t* code_row = a.codes + m * (D / 2);
+  if (!warp_any_nan(vmax)) {
 #pragma unroll
-  for (int j = 0; j < G::NB; ++j) {
-    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
-    store_block(quant_block(xv[2 * j], xv[2 * j + 1], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+      store_block(quant_block_finite(xv[2 * j], xv[2 * j + 1], vmax[2 * j], vmax[2 * j + 1], g, denom), lane_ok, kb,
+                  lane, code_row, sf_rowbase);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+      store_block(quant_block_m(xv[2 * j], xv[2 * j + 1], vmax[2 * j], vmax[2 * j + 1], g, denom), lane_ok, kb,
+                  lane, code_row, sf_rowbase);
+    }
   }
 }
 
@@ -208,9 +228,9 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
 #pragma unroll
     for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
     ss = warp_sum(ss);
-    const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps));
+    const float rinv = __frsqrt_rn(__fadd_rn(mean_of_sum<D>(ss), a.eps));
     const int sel = (!pad && (MUL || ADD) && m / a.rows_per_mod != b0) ? 1 : 0;
-    float am = 0.0f;
+    uint32_t mb[2 * G::NB];
 #pragma unroll
     for (int j = 0; j < G::NB; ++j) {
 #pragma unroll
@@ -218,9 +238,10 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
         const int c = h * (V / 2) + j * 32 + lane;  // vector 2 (j * 32 + lane) + h, half-major
         const uint4 sv = MUL ? s_mod[sel][0][c] : z, hv = ADD ? s_mod[sel][1][c] : z;
         xv[2 * j + h] = norm8<MUL, ADD>(xv[2 * j + h], s_w[c], sv, hv, rinv);
-        am = fmaxf(am, absmax8_fast(xv[2 * j + h]));
+        mb[2 * j + h] = absmax_bits8(xv[2 * j + h]);
       }
     }
+    float am = lane_absmax(xv, mb);
     if (a.y && !pad) {
       uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
 #pragma unroll
@@ -243,10 +264,16 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
     if (lane == 0) a.gs[m] = g;
     const float denom = __fmul_rn(6.0f, g);
     uint8_t* code_row = a.codes + m * (D / 2);
+    if (!warp_any_nan(mb)) {
 #pragma unroll
-    for (int j = 0; j < G::NB; ++j) {
-      const int64_t kb = (int64_t)j * 32 + lane;
-      store_block(quant_block(xv[2 * j], xv[2 * j + 1], g, denom), true, kb, lane, code_row, sf_rowbase);
+      for (int j = 0; j < G::NB; ++j)
+        store_block(quant_block_finite(xv[2 * j], xv[2 * j + 1], mb[2 * j], mb[2 * j + 1], g, denom), true,
+                    (int64_t)j * 32 + lane, lane, code_row, sf_rowbase);
+    } else {
+#pragma unroll
+      for (int j = 0; j < G::NB; ++j)
+        store_block(quant_block_m(xv[2 * j], xv[2 * j + 1], mb[2 * j], mb[2 * j + 1], g, denom), true,
+                    (int64_t)j * 32 + lane, lane, code_row, sf_rowbase);
     }
   }
 }
@@ -291,12 +318,13 @@ __global__ void __launch_bounds__(256) silu_mul_quant_kernel(const SiluArgs a) {
       uv[2 * j + h] = live ? __ldg(urow + c + h) : z;
     }
   }
-  float am = 0.0f;
+  uint32_t mb[2 * G::NB];
 #pragma unroll
   for (int j = 0; j < 2 * G::NB; ++j) {
     gv[j] = silu_mul8(gv[j], uv[j]);
-    am = fmaxf(am, absmax8_fast(gv[j]));
+    mb[j] = absmax_bits8(gv[j]);
   }
+  float am = lane_absmax(gv, mb);
   if (a.y && live) {
     uint4* yrow = reinterpret_cast<uint4*>(a.y + m * a.ldy);
 #pragma unroll
@@ -318,10 +346,20 @@ __global__ void __launch_bounds__(256) silu_mul_quant_kernel(const SiluArgs a) {
   if (wr == 0 && lane == 0) a.gs[m] = g;
   const float denom = __fmul_rn(6.0f, g);
   uint8_t* code_row = a.codes + m * (F / 2);
+  if (!warp_any_nan(mb)) {
 #pragma unroll
-  for (int j = 0; j < G::NB; ++j) {
-    const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
-    store_block(quant_block(gv[2 * j], gv[2 * j + 1], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+      store_block(quant_block_finite(gv[2 * j], gv[2 * j + 1], mb[2 * j], mb[2 * j + 1], g, denom), lane_ok, kb,
+                  lane, code_row, sf_rowbase);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G::NB; ++j) {
+      const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
+      store_block(quant_block_m(gv[2 * j], gv[2 * j + 1], mb[2 * j], mb[2 * j + 1], g, denom), lane_ok, kb, lane,
+                  code_row, sf_rowbase);
+    }
   }
 }
 

@@ -131,15 +131,19 @@ __global__ void __launch_bounds__(256) quantize_blocks_kernel(const __nv_bfloat1
       a[j] = b[j] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  uint32_t ma[G::NB], mb[G::NB];
+#pragma unroll
+  for (int j = 0; j < G::NB; ++j) {
+    ma[j] = absmax_bits8(a[j]);
+    mb[j] = absmax_bits8(b[j]);
+  }
   float g = 0.0f;
   if (GS_MODE == 0) {
     g = gs[0];
   } else if (GS_MODE == 1) {
     g = global_scale(gs[0]);
   } else {
-    float am = 0.0f;
-#pragma unroll
-    for (int j = 0; j < G::NB; ++j) am = fmaxf(am, fmaxf(absmax8_fast(a[j]), absmax8_fast(b[j])));
+    const float am = fmaxf(lane_absmax(a, ma), lane_absmax(b, mb));
     g = global_scale(row_reduce<G::W, true>(am, red, warp, lane));
     if (wr == 0 && lane == 0 && !pad) gs[m] = g;
   }
@@ -153,7 +157,7 @@ __global__ void __launch_bounds__(256) quantize_blocks_kernel(const __nv_bfloat1
 #pragma unroll
   for (int j = 0; j < G::NB; ++j) {
     const int64_t kb = (int64_t)(wr * G::NB + j) * 32 + lane;
-    store_block(quant_block(a[j], b[j], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
+    store_block(quant_block_m(a[j], b[j], ma[j], mb[j], g, denom), lane_ok, kb, lane, code_row, sf_rowbase);
   }
 }
 

@@ -125,18 +125,36 @@ __device__ __forceinline__ uint32_t pack8_finite(uint4 v, float rs) {
   return mag | (c & (nz << 3));
 }
 
-// Largest |x| bit pattern of 16 bf16 values, per half-word: for non-negative IEEE values the
-// bit patterns order like the values, so an unsigned SIMD max gives the absmax exactly;
-// a result above 0x7F80 (infinity) means the block holds a NaN.
-__device__ __forceinline__ uint32_t absmax_bits16(uint4 a, uint4 b) {
+// Largest |x| bit patterns of 8 bf16 values, one per half-word (still packed): for
+// non-negative IEEE values the bit patterns order like the values, so an unsigned SIMD max
+// gives the absmax exactly; a half above 0x7F80 (infinity) means a NaN among its values.
+// The row kernels compute these once per 16-byte vector and use them for both the row's
+// global scale and the 16-element block scales.
+__device__ __forceinline__ uint32_t absmax_bits8(uint4 v) {
   const uint32_t k = 0x7FFF7FFFu;
-  const uint32_t m = __vmaxu2(__vmaxu2(__vmaxu2(a.x & k, a.y & k), __vmaxu2(a.z & k, a.w & k)),
-                              __vmaxu2(__vmaxu2(b.x & k, b.y & k), __vmaxu2(b.z & k, b.w & k)));
-  return max(m & 0xFFFFu, m >> 16);
+  return __vmaxu2(__vmaxu2(v.x & k, v.y & k), __vmaxu2(v.z & k, v.w & k));
+}
+__device__ __forceinline__ uint32_t halves_max(uint32_t m) { return max(m & 0xFFFFu, m >> 16); }
+
+// Absolute maximum of a lane's N vectors (NaN ignored, as the packed max does) from their
+// packed maxima; a lane holding a NaN takes the NaN-ignoring max of every vector instead.
+template <int N>
+__device__ __forceinline__ float lane_absmax(const uint4 (&v)[N], const uint32_t (&mb)[N]) {
+  uint32_t acc = 0u;
+#pragma unroll
+  for (int j = 0; j < N; ++j) acc = __vmaxu2(acc, mb[j]);
+  const uint32_t bits = halves_max(acc);
+  if (bits <= 0x7F80u) return __uint_as_float(bits << 16);
+  float am = 0.0f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) am = fmaxf(am, amax8(v[j]));
+  return am;
 }
 
-__device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float denom) {
-  const uint32_t mb = absmax_bits16(a, b);
+// One 16-element block (vectors a, b with packed maxima ma, mb) -> scale byte + codes.
+__device__ __forceinline__ QBlock quant_block_m(uint4 a, uint4 b, uint32_t ma, uint32_t mbits, float g,
+                                                float denom) {
+  const uint32_t mb = halves_max(__vmaxu2(ma, mbits));
   const bool nan = mb > 0x7F80u;
   // NaN elements do not count towards the block absmax (the packed max ignores them)
   const float am = nan ? fmaxf(amax8(a), amax8(b)) : __uint_as_float(mb << 16);
@@ -151,13 +169,30 @@ __device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float d
   }
   return q;
 }
-
-// Row absmax of finite-or-NaN bf16 data (NaN ignored, as the packed max does): amax of 8 values.
-__device__ __forceinline__ float absmax8_fast(uint4 v) {
-  const uint32_t k = 0x7FFF7FFFu;
-  uint32_t m = __vmaxu2(__vmaxu2(v.x & k, v.y & k), __vmaxu2(v.z & k, v.w & k));
-  m = max(m & 0xFFFFu, m >> 16);
-  return m > 0x7F80u ? amax8(v) : __uint_as_float(m << 16);
+__device__ __forceinline__ QBlock quant_block(uint4 a, uint4 b, float g, float denom) {
+  return quant_block_m(a, b, absmax_bits8(a), absmax_bits8(b), g, denom);
+}
+// The same for a block known to hold no NaN, without a branch: an all-zero block (scale byte
+// 0) gets rs = 0, so every product is (+-)0 and every code the canonical 0, as above.
+__device__ __forceinline__ QBlock quant_block_finite(uint4 a, uint4 b, uint32_t ma, uint32_t mbits, float g,
+                                                     float denom) {
+  const float am = __uint_as_float(halves_max(__vmaxu2(ma, mbits)) << 16);
+  const float s = fminf(__fdiv_rn(am, denom), 448.0f);
+  QBlock q;
+  q.sb = e4m3_rne_sat(s);
+  const float sbf = e4m3_to_f32(q.sb);
+  const float rs = sbf != 0.0f ? __frcp_rn(__fmul_rn(sbf, g)) : 0.0f;
+  q.codes = make_uint2(pack8_finite(a, rs), pack8_finite(b, rs));
+  return q;
+}
+// True when some lane of the warp holds a NaN among the vectors with packed maxima mb[]
+// (warp-uniform, so the block loops that follow, which shuffle, stay converged).
+template <int N>
+__device__ __forceinline__ bool warp_any_nan(const uint32_t (&mb)[N]) {
+  uint32_t acc = 0u;
+#pragma unroll
+  for (int j = 0; j < N; ++j) acc = __vmaxu2(acc, mb[j]);
+  return __any_sync(0xffffffffu, halves_max(acc) > 0x7F80u);
 }
 
 // Lane owns scale block kb of row m (K/16 blocks per row): store its 8 code bytes and, from

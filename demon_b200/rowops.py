@@ -34,6 +34,11 @@ def adanorm_quantize(x: torch.Tensor, norm_w: torch.Tensor, eps: float, scale1: 
     mods = [t for t in (scale1, shift) if t is not None]
     for t in mods:
         _check_cuda_bf16(t, "modulation")
+    for t in mods:
+        # row m uses modulation row m // rows_per_mod: every such row must exist
+        if t.dim() != 2 or t.shape[1] < D or rows_per_mod < 1 or t.shape[0] * rows_per_mod < M:
+            raise ValueError(f"modulation {tuple(t.shape)} must be [ceil(M / rows_per_mod), >= D] "
+                             f"for M={M}, D={D}, rows_per_mod={rows_per_mod}")
     multi = [t for t in mods if t.shape[0] > 1]   # a single row's stride is irrelevant
     ld_mod = multi[0].stride(0) if multi else (D if mods else 0)
     if any(t.stride(1) != 1 for t in mods) or any(t.stride(0) != ld_mod for t in multi):

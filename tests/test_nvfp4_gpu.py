@@ -78,6 +78,28 @@ def test_quantize_edge_values(cuda):
         assert np.array_equal(q.sf.cpu().numpy(), ref_swz), f"scales mode {mode}"
 
 
+@pytest.mark.parametrize("K", [2048, 6144])
+def test_quantize_nan_values(cuda, K):
+    """NaN elements do not count towards any absmax (row or block) and get code 0 -- the
+    quantiser's slow path, taken by a whole warp when one of its lanes holds a NaN; rows
+    without a NaN next to them take the fast path.  Bit-exact against the oracle."""
+    from demon_b200 import nvfp4
+    rng = np.random.default_rng(K)
+    M = 40
+    x = (rng.standard_normal((M, K)) * 2.0).astype(np.float32)
+    mask = rng.random((M, K)) < 0.003
+    mask[::5] = False                     # some rows hold no NaN at all
+    x[mask] = np.nan
+    xb = O.f32_to_bf16_bits(x)
+    xt = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16)
+    for mode in (1, 2):
+        ref_codes, ref_swz, _, ref_gs = O.quantize(xb, mode, None)
+        q = nvfp4.quantize(xt.to(cuda), gs_mode=mode)
+        assert np.array_equal(q.codes.cpu().numpy(), ref_codes), f"codes mode {mode}"
+        assert np.array_equal(q.sf.cpu().numpy(), ref_swz), f"scales mode {mode}"
+        assert np.array_equal(q.gs.cpu().numpy().view(np.uint32), np.asarray(ref_gs, np.float32).view(np.uint32))
+
+
 def _dequant_ref(q_codes, q_sf, gs, rows, K):
     lin = O.unswizzle_sf(q_sf, rows, K)
     return torch.from_numpy(O.dequantize(q_codes, lin, gs))

@@ -231,3 +231,17 @@ def test_gemm_silu_epilogue(cuda, M, F, bias):
     # and against the definition on the GEMM's own gate / up values
     gf, uf = gu[:, :F].float().cpu(), gu[:, F:].float().cpu()
     ulp_check(h, bf(bf(gf / (1 + torch.exp(-gf))) * uf))
+
+
+def test_adanorm_rejects_short_modulation(cuda):
+    """Row m reads modulation row m // rows_per_mod: a table with too few rows is refused on the
+    host before any launch (the C ABI is given only its pointer and row pitch)."""
+    from demon_b200.rowops import adanorm_quantize
+    M, D, S = 1500, 2048, 750
+    x = torch.zeros(M, D, dtype=torch.bfloat16, device=cuda)
+    w = torch.ones(D, dtype=torch.bfloat16, device=cuda)
+    short = torch.ones(1, D, dtype=torch.bfloat16, device=cuda)   # needs M / S = 2 rows
+    with pytest.raises(ValueError, match="modulation"):
+        adanorm_quantize(x, w, 1e-6, short, short, S)
+    ok = torch.ones(2, D, dtype=torch.bfloat16, device=cuda)
+    adanorm_quantize(x, w, 1e-6, ok, ok, S)
