@@ -244,6 +244,16 @@ __device__ __forceinline__ void ld_global_row64(const void* p, uint4 (&r)[4]) {
                  : "l"(reinterpret_cast<const uint8_t*>(p) + 16 * j));
 }
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+// 16-byte asynchronous global -> shared copy through L2 (LSU path, not the TMA unit)
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// The barrier's pending count goes up by one now and down by one when this thread's earlier
+// cp.async copies have landed: a phase cannot complete before them.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N bulk groups of this thread still read their shared-memory source.

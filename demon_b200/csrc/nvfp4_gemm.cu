@@ -79,10 +79,17 @@ struct GemmParams {
 constexpr int kBM = 128;
 constexpr int kRowBytes = 128;   // one 128-byte swizzle row per stage (256 fp4 / 64 bf16)
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+// Warpgroup 0: the TMA producer (warp 0), the MMA issuer (warp 1) and two idle warps; warpgroups
+// 1-2: the epilogue.  setmaxnreg moves registers from warpgroup 0 to the epilogue, whose loads of
+// the gate, residual and rotary tables are kept in flight a step ahead of their use:
+// 128 * 56 + 256 * 224 = 64,512 = 384 * 168, the launch's registers.
+constexpr int kThreads = 128 + 32 * kEpiWarps;
+constexpr int kGemmLaunchRegs = 168, kGemmIssueRegs = 56, kGemmEpiRegs = 224;
+static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads * kGemmLaunchRegs,
+              "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
-template <int BN, int STAGES, bool FP4, bool PAIR = false>
+template <int BN, int STAGES, bool FP4, bool PAIR = false, bool SIDE = false>
 struct GemmCfg {
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
@@ -95,10 +102,17 @@ struct GemmCfg {
   // per epilogue warp: two 2 KB TMA-store staging buffers (FP4), or one transpose block (bf16)
   static constexpr int kStgWarp = FP4 ? 4096 : 32 * kStgPitch;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
-  static constexpr int offCol = offStg + kEpiWarps * kStgWarp;  // fp32 per-column vector per warp
+  // side-input tile (SIDE kernels), loaded once per tile by a loader warp and read row by row:
+  // the rotary tables of the CTA's 128 rows (cos rows, then sin rows: 256 bytes at a 272-byte
+  // pitch, so that a warp's row-per-lane 16-byte reads are conflict-free), or the residual tile
+  // (four 128-row x 64-column TMA boxes with the 128-byte swizzle)
+  static constexpr int kSideRow = 272;
+  static constexpr int kSide = SIDE ? 2 * kBM * kSideRow : 0;
+  static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
+  static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
   static constexpr int offHn = offCol + kEpiWarps * (BN / 2) * 4;  // fp32 head-norm weight per warp
   static constexpr int offBar = offHn + (FP4 ? kEpiWarps * (BN / 2) * 4 : 0);
-  static constexpr int kBars = 2 * STAGES + 3;
+  static constexpr int kBars = 2 * STAGES + 3 + (SIDE ? 2 : 0);
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
   static constexpr int kSfaCol = BN;                 // 4 columns per K=64 step, 4 steps
@@ -111,6 +125,7 @@ struct GemmCfg {
   static constexpr int kChunks = kColsPerWarp / 32;  // 32-column chunks per epilogue warp
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(!SIDE || (FP4 && BN == 256 && offSide % 1024 == 0 && kSide >= 4 * kBM * 128), "side tile");
 };
 
 // Tile t -> (m_blk, n_blk).  Tiles run in bands of m_group m-blocks: inside a band the
@@ -139,13 +154,14 @@ __device__ __forceinline__ int stg_off(int r, int j) { return r * 64 + ((j ^ ((r
 
 // One CTA per SM (persistent).  10 warps spread over the SM's 4 sub-partitions put 3 warps on
 // two of them, so a thread gets at most 168 of a sub-partition's 16 K registers.
-template <int BN, int STAGES, bool FP4, bool PAIR>
+template <int BN, int STAGES, bool FP4, bool PAIR, bool SIDE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
                 const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmSFA,
-                const __grid_constant__ CUtensorMap tmSFB, const GemmParams p) {
-  using C = GemmCfg<BN, STAGES, FP4, PAIR>;
+                const __grid_constant__ CUtensorMap tmSFB, const __grid_constant__ CUtensorMap tmR,
+                const GemmParams p) {
+  using C = GemmCfg<BN, STAGES, FP4, PAIR, SIDE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::offBar);
@@ -153,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
+  uint64_t* side_full = mma_done + 1;   // SIDE kernels only
+  uint64_t* side_empty = mma_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::offMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::offMisc + 4);
 
@@ -180,6 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);  // the pair's epilogue warps
     mbar_init(mma_done, 1);
+    if (SIDE) {
+      mbar_init(side_full, 1);
+      mbar_init(side_empty, kEpiWarps);  // this CTA's epilogue warps
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -211,8 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-
-  if (warp == 0) {
+  if (warp < 4) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kGemmIssueRegs));
+   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
       uint32_t g = 0;  // stages issued so far (all tiles)
@@ -394,9 +417,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9, lim);
     }
     __syncwarp();
+   } else if (SIDE && warp == 2) {
+    // ------------------------------------------------------------ side-input loader
+    // Per tile that needs it (every tile for the residual, tiles with normed heads for the
+    // rotary tables), once the epilogue warps have read the previous one: the table rows by
+    // coalesced 16-byte cp.async copies, half a warp per 256-byte row (positions wrap at
+    // rope_S inside a tile; rows past M are skipped), or the residual tile by four TMA boxes
+    // (rows past M read as zeros).
+    const bool side_rope = p.rope_cos != nullptr;
+    uint8_t* side = smem + C::offSide;
+    uint32_t sit = 0;  // side tiles issued
+    for (int tile = cid; tile < num_tiles; tile += ncl) {
+      int m_blk, n_blk;
+      tile_coords(tile, p, m_blk, n_blk);
+      const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;
+      if (side_rope && n0 >= p.hn_cols) continue;
+      if (!mbar_wait(side_empty, (sit & 1u) ^ 1u, abort_flag, t0, p.status, 10, lim)) break;
+      if (side_rope) {
+        const int rows = max(0, min(kBM, p.M - m0));
+        const int hl = lane >> 4, ch = lane & 15;  // row parity, 16-byte chunk of the row
+        const uint32_t sb = smem_u32(side);
+        int64_t pos = ((int64_t)m0 + hl) % p.rope_S;
+        for (int r = hl; r < rows; r += 2) {
+          cp_async_16(sb + r * C::kSideRow + ch * 16, p.rope_cos + pos * 128 + ch * 8);
+          cp_async_16(sb + (kBM + r) * C::kSideRow + ch * 16, p.rope_sin + pos * 128 + ch * 8);
+          pos += 2;
+          while (pos >= p.rope_S) pos -= p.rope_S;
+        }
+        cp_async_mbar_arrive(side_full);  // every lane's copies are part of this phase
+        __syncwarp();
+        if (lane == 0) mbar_arrive(side_full);
+      } else if (lane == 0) {
+        mbar_arrive_expect_tx(side_full, 4u * kBM * 128u);
+        for (int b = 0; b < 4; ++b) tma_load_2d(side + b * (kBM * 128), &tmR, side_full, n0 + 64 * b, m0);
+      }
+      __syncwarp();
+      ++sit;
+    }
+    // the CTA leaves only after its last side copy has landed (it may not have been read)
+    if (sit > 0) {
+      volatile int never = 0;
+      mbar_wait(side_full, (sit - 1u) & 1u, &never, globaltimer(), p.status, 11, lim);
+    }
+    __syncwarp();
+   }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kGemmEpiRegs));
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;            // 0..7
+    const int ew = warp - 4;            // 0..7
     const int q = warp & 3;             // TMEM lane quadrant accessible to this warp
     const int half = ew >> 2;           // which half of the tile's columns
     const uint32_t stg = smem_u32(smem + C::offStg + ew * C::kStgWarp);
@@ -405,6 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     const uint64_t out_policy = l2_policy_evict_first();
     uint32_t it = 0, nstore = 0;
+    // SIDE kernels: the rotary tables (head norm + RoPE) or the residual come from the side tile
+    const bool side_rope = SIDE && p.rope_cos != nullptr;
+    const bool side_res = SIDE && !side_rope;
+    const uint32_t side = smem_u32(smem + C::offSide);
+    uint32_t sit = 0;  // side tiles consumed
     // SwiGLU: a BN = 256 tile holds gate block n and up block n of the interleaved weight; each
     // warp takes 64 output columns (its 64 gate and the matching 64 up accumulator columns)
     const bool sm = FP4 && BN == 256 && p.silu_mul != 0;
@@ -413,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(tile, p, m_blk, n_blk);
       const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;  // this CTA's 128 rows
       const int ncol0 = n0 + half * C::kColsPerWarp;
+      const bool need_side = SIDE && (side_rope ? n0 < p.hn_cols : true);
       // Everything that does not depend on the accumulator is fetched while the MMAs run:
       // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
       // the lane's row scale, and L2 prefetches of its gate / residual row segments.
@@ -438,12 +512,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float alpha_u = sm ? a_row * p.w_gs[p.w_gs_per_block ? wblk + 1 : 0] : alpha;
       const __nv_bfloat16* gate_row =
           (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
-      const __nv_bfloat16* res_row = (FP4 && p.residual && row_ok) ? p.residual + row * p.ldr + ncol0 : nullptr;
+      const __nv_bfloat16* res_row =
+          (FP4 && p.residual && row_ok && !side_res) ? p.residual + row * p.ldr + ncol0 : nullptr;
 #pragma unroll
       for (int j = 0; j < C::kColsPerWarp * 2; j += 128) {
         if (gate_row) prefetch_l2(reinterpret_cast<const uint8_t*>(gate_row) + j);
         if (res_row) prefetch_l2(reinterpret_cast<const uint8_t*>(res_row) + j);
       }
+      if (gate_row) prefetch_l1(gate_row);  // the first 32-column chunk's segments into L1
+      if (res_row) prefetch_l1(res_row);
       __syncwarp();
       if (!mbar_wait(acc_full, it & 1u, abort_flag, t0, p.status, 7, lim)) break;
       tc_fence_after();
@@ -504,6 +581,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < 16; ++k) y[c][k] = silu_mul_bf2(y[c][k], y[c + 2][k]);
         }
       }
+      // rotary tables of the row's position: their cache lines are pulled into L1 ahead of use
+      // (no registers held), the first 64-column half's here, while the head norm runs
+      const __nv_bfloat16* cos_row =
+          (hn && p.rope_cos && !side_rope) ? p.rope_cos + (row % p.rope_S) * 128 : nullptr;
+      const __nv_bfloat16* sin_row =
+          (hn && p.rope_cos && !side_rope) ? p.rope_sin + (row % p.rope_S) * 128 : nullptr;
+      if (cos_row) {
+        prefetch_l1(cos_row);
+        prefetch_l1(cos_row + 64);
+        prefetch_l1(sin_row);
+        prefetch_l1(sin_row + 64);
+      }
+      if (need_side && !mbar_wait(side_full, sit & 1u, abort_flag, t0, p.status, 12, lim)) break;
+      const int srow = q * 32 + lane;  // the lane's row in the side tile
       if (hn) {
         // q_norm / k_norm: Qwen3RMSNorm over the row's 128 values of this head
         float2 s2 = make_float2(0.0f, 0.0f);
@@ -531,12 +622,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t pos = row % p.rope_S;
           const uint4* cr = reinterpret_cast<const uint4*>(p.rope_cos + pos * 128);
           const uint4* sr = reinterpret_cast<const uint4*>(p.rope_sin + pos * 128);
+          const uint32_t cb = side + srow * C::kSideRow, sb = side + (kBM + srow) * C::kSideRow;
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint4 c1 = __ldg(cr + c * 4 + j), c2 = __ldg(cr + 8 + c * 4 + j);
-              const uint4 s1 = __ldg(sr + c * 4 + j), s2v = __ldg(sr + 8 + c * 4 + j);
+              uint4 c1, c2, s1, s2v;
+              if (side_rope) {
+                c1 = ld_shared_v4(cb + (c * 4 + j) * 16);
+                c2 = ld_shared_v4(cb + (8 + c * 4 + j) * 16);
+                s1 = ld_shared_v4(sb + (c * 4 + j) * 16);
+                s2v = ld_shared_v4(sb + (8 + c * 4 + j) * 16);
+              } else {
+                c1 = __ldg(cr + c * 4 + j);
+                c2 = __ldg(cr + 8 + c * 4 + j);
+                s1 = __ldg(sr + c * 4 + j);
+                s2v = __ldg(sr + 8 + c * 4 + j);
+              }
               const uint32_t cw1[4] = {c1.x, c1.y, c1.z, c1.w}, cw2[4] = {c2.x, c2.y, c2.z, c2.w};
               const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w}, sw2[4] = {s2v.x, s2v.y, s2v.z, s2v.w};
 #pragma unroll
@@ -551,6 +653,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
         if (sm && c >= 2) break;  // SwiGLU: two 32-column output chunks per warp
+        if (c + 1 < C::kChunks) {  // the next chunk's gate / residual segments into L1
+          if (gate_row) prefetch_l1(gate_row + (c + 1) * 32);
+          if (res_row) prefetch_l1(res_row + (c + 1) * 32);
+        }
         const int ncol = sm ? (n0 >> 1) + half * 64 + c * 32 : ncol0 + c * 32;
         // FP4 tiles never cross N (N % BN == 0); the bf16 GEMM's last tile can (rank < BN)
         if (!FP4 && ncol >= p.N) break;
@@ -565,9 +671,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 4; ++i) y[c][4 * j + i] = mul_bf2(y[c][4 * j + i], gw[i]);
             }
           }
-          if (res_row) {  // out = bf16(residual + y)
+          if (res_row || side_res) {  // out = bf16(residual + y)
             uint4 rx[4];
-            ld_global_row64(res_row + c * 32, rx);
+            if (side_res) {  // box half * 2 + c / 2, 16-byte chunk k of the row at k ^ (row & 7)
+              const uint32_t rb = side + (half * 2 + (c >> 1)) * (kBM * 128) + srow * 128;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) rx[j] = ld_shared_v4(rb + ((((c & 1) * 4 + j) ^ (srow & 7)) << 4));
+            } else {
+              ld_global_row64(res_row + c * 32, rx);
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
@@ -615,6 +727,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
       }
+      if (need_side) {  // every lane has read its side rows: the loader may refill the tile
+        __syncwarp();
+        if (lane == 0) mbar_arrive(side_empty);
+        ++sit;
+      }
     }
     if (FP4 && lane == 0) bulk_wait_all();  // the staging buffers stay valid until every store has read them
     __syncwarp();
@@ -636,14 +753,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 constexpr int kBandMBlocks = 8;
 
-template <int BN, int STAGES, bool FP4, bool PAIR = false>
+template <int BN, int STAGES, bool FP4, bool PAIR = false, bool SIDE = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
                 const CUtensorMap& o, GemmParams p, cudaStream_t st, const CUtensorMap* sfa = nullptr,
-                const CUtensorMap* sfb = nullptr) {
-  using C = GemmCfg<BN, STAGES, FP4, PAIR>;
-  auto kern = gemm_kernel<BN, STAGES, FP4, PAIR>;
+                const CUtensorMap* sfb = nullptr, const CUtensorMap* res = nullptr) {
+  using C = GemmCfg<BN, STAGES, FP4, PAIR, SIDE>;
+  auto kern = gemm_kernel<BN, STAGES, FP4, PAIR, SIDE>;
   static std::atomic<uint64_t> attr_done{0};
   if (device_pending(attr_done)) {
+    // the warpgroups' register split adds up to the launch's registers; with any other count
+    // per thread at launch the epilogue's setmaxnreg.inc would never return
+    cudaFuncAttributes fa;
+    DEMON_CUDA(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs != kGemmLaunchRegs) {
+      set_error("gemm: kernel built with %d registers per thread, the register split needs %d", fa.numRegs,
+                kGemmLaunchRegs);
+      return DEMON_ERR_CUDA;
+    }
     DEMON_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     mark_device_done(attr_done);
   }
@@ -662,7 +788,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   memset(&z, 0, sizeof z);
   if (!PAIR) {
     const dim3 grid((unsigned)std::min(tiles, sms));
-    kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, o, z, z, p);
+    kern<<<grid, kThreads, C::kSmem, st>>>(a, b, la, lb, o, z, z, z, p);
     DEMON_CUDA(cudaGetLastError());
     return DEMON_OK;
   }
@@ -679,7 +805,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  DEMON_CUDA(cudaLaunchKernelEx(&cfg, kern, a, b, la, lb, o, sfa ? *sfa : z, sfb ? *sfb : z, p));
+  DEMON_CUDA(cudaLaunchKernelEx(&cfg, kern, a, b, la, lb, o, sfa ? *sfa : z, sfb ? *sfb : z, res ? *res : z, p));
   return DEMON_OK;
 }
 
@@ -688,6 +814,13 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
 namespace demon {
 // CTA-pair tiles are the default for N % 256 == 0; DEMON_GEMM_PAIR=0 selects the one-CTA
 // kernel (kept for comparison and as the N % 256 != 0 path).
+static bool side_stage_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("DEMON_GEMM_SIDE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 static bool pair_gemm_enabled() {
   static const bool on = [] {
     const char* e = getenv("DEMON_GEMM_PAIR");
@@ -845,6 +978,20 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
     t_stall_wait_ns = 0;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // A side tile (three stages instead of four, for its 68 KB of shared memory) when the
+  // epilogue would otherwise read per-row operands one row per lane: the rotary tables of
+  // the head-norm + RoPE epilogue, or the residual (its rows 16-byte aligned)
+  const bool side_rope = a->rope_cos && a->hn_cols > 0;
+  const bool side_res = !side_rope && a->residual && !silu && ((uintptr_t)a->residual & 15) == 0 &&
+                        (a->ldr * 2) % 16 == 0;
+  if (pair && side_stage_enabled() && (side_rope || side_res)) {
+    CUtensorMap tr;
+    memset(&tr, 0, sizeof tr);
+    if (side_res)
+      DEMON_RC(make_tmap_2d(&tr, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                            (uint64_t)a->ldr * 2, 64, 128));
+    return launch_gemm<256, 3, true, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb, &tr);
+  }
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
   return launch_gemm<128, 5, true>(ta, tb, tla, tlb, to, p, st);
