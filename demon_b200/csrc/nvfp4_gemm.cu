@@ -68,6 +68,9 @@ struct GemmParams {
   float hn_eps;
   int m_tiles, n_tiles;
   int m_group;  // tile order: bands of m_group m-blocks, each swept over every n-block
+  // > 0: CTA (pair) c takes the contiguous tiles [c * tile_chunk, (c + 1) * tile_chunk) instead
+  // of every ncl-th tile; with m_group = 1 it sweeps N over one m-block before the next
+  int tile_chunk;
   int silu_mul;  // SwiGLU epilogue: interleaved gate/up blocks of 128 -> h of width N / 2
   // bounded-wait test (demon_test_arm_gemm_stall): the first CTA (pair) waits at most wait_ns
   // and its rank-0 CTA withholds the loads of its first stage; 0 in normal launches
@@ -186,6 +189,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cid = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int ncl = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr int kTileM = PAIR ? 2 * kBM : kBM;
+  // this CTA's tiles: t_begin, t_begin + t_step, ... < t_end (every role walks the same list)
+  const int t_begin = p.tile_chunk ? cid * p.tile_chunk : cid;
+  const int t_step = p.tile_chunk ? 1 : ncl;
+  const int t_end = p.tile_chunk ? min(num_tiles, t_begin + p.tile_chunk) : num_tiles;
+  // SIDE kernels: the side tile a tile reads, as a key (-1: none).  The rotary tables depend
+  // on the rows only, so consecutive tiles of one m-block share one load; a residual tile is
+  // its own.  A side tile is released after the last of a run of tiles with its key.
+  auto side_key = [&](int tile) -> int {
+    if (!SIDE || tile >= t_end) return -1;
+    int mb, nb;
+    tile_coords(tile, p, mb, nb);
+    if (p.rope_cos) return nb * BN < p.hn_cols ? mb : -1;
+    return tile;
+  };
   // wait limit of this CTA: the default, or the armed test's short one in the first CTA (pair)
   const uint64_t lim = (p.withhold && cid == 0) ? p.wait_ns : (uint64_t)DEMON_WAIT_LIMIT_NS;
   const bool hold0 = p.withhold && cid == 0 && rank == 0;  // test: skip the loads of stage 0
@@ -241,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;  // stages issued so far (all tiles)
       const int64_t kchunks = p.K / 64;
       bool ok = true;
-      for (int tile = cid; ok && tile < num_tiles; tile += ncl) {
+      for (int tile = t_begin; ok && tile < t_end; tile += t_step) {
         int m_blk, n_blk;
         tile_coords(tile, p, m_blk, n_blk);
         const int m0 = m_blk * kTileM, n0 = n_blk * BN;
@@ -311,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ib = idesc_bf16(kTileM, BN);
       uint32_t g = 0, it = 0;
       bool ok = true;
-      for (int tile = cid; ok && tile < num_tiles; tile += ncl, ++it) {
+      for (int tile = t_begin; ok && tile < t_end; tile += t_step, ++it) {
         // the epilogue must have drained the previous tile's accumulator; without hot LoRA the
         // first stage's scale-factor copies are issued before that wait
         const bool early_sf = FP4 && lboxes == 0;
@@ -419,19 +436,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
    } else if (SIDE && warp == 2) {
     // ------------------------------------------------------------ side-input loader
-    // Per tile that needs it (every tile for the residual, tiles with normed heads for the
-    // rotary tables), once the epilogue warps have read the previous one: the table rows by
-    // coalesced 16-byte cp.async copies, half a warp per 256-byte row (positions wrap at
-    // rope_S inside a tile; rows past M are skipped), or the residual tile by four TMA boxes
-    // (rows past M read as zeros).
+    // At the first tile of each run of tiles with one side key, once the epilogue warps have
+    // released the previous side tile: the table rows of the m-block by coalesced 16-byte
+    // cp.async copies, half a warp per 256-byte row (positions wrap at rope_S inside a tile;
+    // rows past M are skipped), or the residual tile by four TMA boxes (rows past M read as
+    // zeros).
     const bool side_rope = p.rope_cos != nullptr;
     uint8_t* side = smem + C::offSide;
     uint32_t sit = 0;  // side tiles issued
-    for (int tile = cid; tile < num_tiles; tile += ncl) {
+    int loaded = -1;   // key of the side tile in shared memory (-1: released)
+    for (int tile = t_begin; tile < t_end; tile += t_step) {
+      const int key = side_key(tile);
+      if (key < 0) continue;
+      const bool fresh = key != loaded;
+      loaded = side_key(tile + t_step) == key ? key : -1;  // the epilogue releases at a run's end
+      if (!fresh) continue;
       int m_blk, n_blk;
       tile_coords(tile, p, m_blk, n_blk);
       const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;
-      if (side_rope && n0 >= p.hn_cols) continue;
       if (!mbar_wait(side_empty, (sit & 1u) ^ 1u, abort_flag, t0, p.status, 10, lim)) break;
       if (side_rope) {
         const int rows = max(0, min(kBM, p.M - m0));
@@ -477,16 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool side_rope = SIDE && p.rope_cos != nullptr;
     const bool side_res = SIDE && !side_rope;
     const uint32_t side = smem_u32(smem + C::offSide);
-    uint32_t sit = 0;  // side tiles consumed
+    uint32_t sit = 0;  // side tiles released
+    int cur = -1;      // key of the side tile this warp has seen land (-1: none)
     // SwiGLU: a BN = 256 tile holds gate block n and up block n of the interleaved weight; each
     // warp takes 64 output columns (its 64 gate and the matching 64 up accumulator columns)
     const bool sm = FP4 && BN == 256 && p.silu_mul != 0;
-    for (int tile = cid; tile < num_tiles; tile += ncl, ++it) {
+    for (int tile = t_begin; tile < t_end; tile += t_step, ++it) {
       int m_blk, n_blk;
       tile_coords(tile, p, m_blk, n_blk);
       const int m0 = m_blk * kTileM + (int)rank * kBM, n0 = n_blk * BN;  // this CTA's 128 rows
       const int ncol0 = n0 + half * C::kColsPerWarp;
-      const bool need_side = SIDE && (side_rope ? n0 < p.hn_cols : true);
+      const int skey = side_key(tile);
+      const bool need_side = skey >= 0;
       // Everything that does not depend on the accumulator is fetched while the MMAs run:
       // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
       // the lane's row scale, and L2 prefetches of its gate / residual row segments.
@@ -593,7 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_l1(sin_row);
         prefetch_l1(sin_row + 64);
       }
-      if (need_side && !mbar_wait(side_full, sit & 1u, abort_flag, t0, p.status, 12, lim)) break;
+      if (need_side && skey != cur) {
+        if (!mbar_wait(side_full, sit & 1u, abort_flag, t0, p.status, 12, lim)) break;
+        cur = skey;
+      }
       const int srow = q * 32 + lane;  // the lane's row in the side tile
       if (hn) {
         // q_norm / k_norm: Qwen3RMSNorm over the row's 128 values of this head
@@ -727,10 +754,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
       }
-      if (need_side) {  // every lane has read its side rows: the loader may refill the tile
+      if (need_side && side_key(tile + t_step) != skey) {  // end of the run: release the side tile
         __syncwarp();
         if (lane == 0) mbar_arrive(side_empty);
         ++sit;
+        cur = -1;
       }
     }
     if (FP4 && lane == 0) bulk_wait_all();  // the staging buffers stay valid until every store has read them
@@ -784,6 +812,14 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   // large-M launches sweep N in bands of 8 m-blocks; smaller ones keep m-fastest order
   const double a_bytes = (double)p.M * p.K * (FP4 ? 0.5625 : 2.0);
   p.m_group = (a_bytes > 24e6) ? std::min(p.m_tiles, kBandMBlocks) : p.m_tiles;
+  if (SIDE && p.rope_cos) {
+    // each pair sweeps N over its own m-blocks (contiguous tiles, n fastest): the rotary
+    // tables of an m-block are loaded once for all its head tiles; the pairs' A blocks
+    // (256 KB each) stay in L2 while they are swept
+    const int pairs = std::min(tiles, sms / 2);
+    p.m_group = 1;
+    p.tile_chunk = (tiles + pairs - 1) / pairs;
+  }
   CUtensorMap z;
   memset(&z, 0, sizeof z);
   if (!PAIR) {
@@ -980,10 +1016,10 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // A side tile (three stages instead of four, for its 68 KB of shared memory) when the
   // epilogue would otherwise read per-row operands one row per lane: the rotary tables of
-  // the head-norm + RoPE epilogue, or the residual (its rows 16-byte aligned)
+  // the head-norm + RoPE epilogue, or the residual (gemm_check: never both, never with
+  // SwiGLU; residual rows 16-byte aligned)
   const bool side_rope = a->rope_cos && a->hn_cols > 0;
-  const bool side_res = !side_rope && a->residual && !silu && ((uintptr_t)a->residual & 15) == 0 &&
-                        (a->ldr * 2) % 16 == 0;
+  const bool side_res = a->residual != nullptr;
   if (pair && side_stage_enabled() && (side_rope || side_res)) {
     CUtensorMap tr;
     memset(&tr, 0, sizeof tr);

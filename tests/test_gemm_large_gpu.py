@@ -160,3 +160,76 @@ def test_head_norm_rope_epilogue_at_tick_size(cuda):
         ref[:, h * 128:(h + 1) * 128] = nrm * c + rot * s
     err = rel_fro(y[rd].cpu(), ref)
     assert err <= REL_FRO_TOL, err
+
+
+def test_gated_residual_epilogue_at_tick_size(cuda):
+    """The attention output projection's epilogue at 96,000 x 2048 x 2048: out = residual +
+    gate[row // 750] * y, the residual read from the side tile.  Whole sequences against the
+    same sequences alone (bit-exact) and against fp64."""
+    from demon_b200 import nvfp4
+    M, N, K = MT, 2048, 2048
+    x = big_x(M, K, seed=21, dev=cuda)
+    w = nvfp4.pack_weight(weight(N, K, seed=22, std=0.05, dev=cuda))
+    g = torch.Generator(device=cuda).manual_seed(23)
+    res = torch.randn(M, N, generator=g, device=cuda).to(torch.bfloat16)
+    gate = torch.randn(M // S_TOK, N, generator=g, device=cuda).to(torch.bfloat16)
+    y = nvfp4.gemm(nvfp4.quantize(x), w, residual=res, gate=gate, gate_rows=S_TOK)
+    seqs = [0, 77, M // S_TOK - 1]
+    rows = torch.cat([torch.arange(s * S_TOK, (s + 1) * S_TOK) for s in seqs])
+    rd = rows.to(cuda)
+    a_s = nvfp4.quantize(x[rd].contiguous())
+    small = nvfp4.gemm(a_s, w, residual=res[rd].contiguous(), gate=gate[seqs].contiguous(), gate_rows=S_TOK)
+    assert torch.equal(y[rd], small)
+    lin = dequant_rows(a_s, torch.arange(len(rows))) @ dequant_all(w).T
+    gr = gate[seqs].double().cpu().repeat_interleave(S_TOK, 0)
+    ref = res[rd].double().cpu() + gr * lin
+    err = rel_fro(y[rd].cpu(), ref)
+    assert err <= REL_FRO_TOL, err
+
+
+_DIRECT_PATH_CHILD = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from demon_b200 import nvfp4 as Q
+dev = torch.device("cuda", 0)
+g = torch.Generator(device=dev).manual_seed(5)
+M, K, S, hq, hk = 3001, 512, 750, 4, 2
+x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+a = Q.quantize(x)
+w1 = Q.pack_weight((torch.randn(768, K, generator=g, device=dev) * 0.05).to(torch.bfloat16))
+big = torch.randn(M, 1024, generator=g, device=dev).to(torch.bfloat16)
+res = big[:, 128:896]                                   # row pitch 1024 > N = 768
+gate = torch.randn(M // 7 + 1, 768, generator=g, device=dev).to(torch.bfloat16)
+wqkv = Q.pack_weight((torch.randn((hq + 2 * hk) * 128, K, generator=g, device=dev) * 0.05).to(torch.bfloat16))
+wq = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+wk = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+cos = torch.randn(S, 128, generator=g, device=dev).to(torch.bfloat16)
+sin = torch.randn(S, 128, generator=g, device=dev).to(torch.bfloat16)
+out = {
+    "res": Q.gemm(a, w1, residual=res, gate=gate, gate_rows=7),
+    "res_plain": Q.gemm(a, w1, residual=res),
+    "rope": Q.gemm(a, wqkv, head_norm=((hq + hk) * 128, hq * 128, wq, wk, 1e-6), rope=(cos, sin, S)),
+}
+torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[2])
+"""
+
+
+def test_side_tile_matches_direct_path(cuda, tmp_path):
+    """The epilogue's side tile (rotary rows by cp.async, residual by TMA boxes, three
+    pipeline stages) and the direct per-lane reads (DEMON_GEMM_SIDE=0, four stages) give the
+    same bits: a strided residual with a per-7-rows gate, and head norm + RoPE whose positions
+    wrap inside tiles, at an M that leaves the last CTA pair partly empty."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = str(Path(__file__).resolve().parents[1])
+    outs = {}
+    for side in ("1", "0"):
+        f = tmp_path / f"side{side}.pt"
+        env = dict(os.environ, DEMON_GEMM_SIDE=side)
+        subprocess.run([sys.executable, "-c", _DIRECT_PATH_CHILD, root, str(f)], env=env, check=True, timeout=600)
+        outs[side] = torch.load(f)
+    for k in outs["1"]:
+        assert torch.isfinite(outs["1"][k]).all(), k
+        assert torch.equal(outs["1"][k], outs["0"][k]), k
