@@ -92,7 +92,8 @@ static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads *
               "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
-template <int BN, int STAGES, bool FP4, bool PAIR = false, bool SIDE = false>
+// SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual
+template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 struct GemmCfg {
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
@@ -102,19 +103,22 @@ struct GemmCfg {
   static constexpr int offB = offA + STAGES * kA;
   static constexpr int offSFA = offB + STAGES * kB;
   static constexpr int offSFB = offSFA + STAGES * kSFA;
-  // per epilogue warp: two 2 KB TMA-store staging buffers (FP4), or one transpose block (bf16)
-  static constexpr int kStgWarp = FP4 ? 4096 : 32 * kStgPitch;
+  // per epilogue warp: two 2 KB TMA-store staging buffers (FP4), or one transpose block (bf16);
+  // none with the residual side tile, whose rows the output overwrites and is stored from
+  static constexpr int kStgWarp = SIDE == 2 ? 0 : FP4 ? 4096 : 32 * kStgPitch;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
-  // side-input tile (SIDE kernels), loaded once per tile by a loader warp and read row by row:
-  // the rotary tables of the CTA's 128 rows (cos rows, then sin rows: 256 bytes at a 272-byte
-  // pitch, so that a warp's row-per-lane 16-byte reads are conflict-free), or the residual tile
-  // (four 128-row x 64-column TMA boxes with the 128-byte swizzle)
+  // side-input tile (SIDE kernels), loaded by a loader warp and read row by row: the rotary
+  // tables of the CTA's 128 rows (cos rows, then sin rows: 256 bytes at a 272-byte pitch, so
+  // that a warp's row-per-lane 16-byte reads are conflict-free), or the residual tile (four
+  // 128-row x 64-column TMA boxes with the 128-byte swizzle) and the tile's segments of the
+  // (at most two) gate rows its 128 rows use
   static constexpr int kSideRow = 272;
-  static constexpr int kSide = SIDE ? 2 * kBM * kSideRow : 0;
+  static constexpr int kSideGate = 4 * kBM * 128;  // offset of the gate segments (SIDE 2)
+  static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 : 0;
   static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
   static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
   static constexpr int offHn = offCol + kEpiWarps * (BN / 2) * 4;  // fp32 head-norm weight per warp
-  static constexpr int offBar = offHn + (FP4 ? kEpiWarps * (BN / 2) * 4 : 0);
+  static constexpr int offBar = offHn + (FP4 && SIDE != 2 ? kEpiWarps * (BN / 2) * 4 : 0);
   static constexpr int kBars = 2 * STAGES + 3 + (SIDE ? 2 : 0);
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
@@ -128,7 +132,7 @@ struct GemmCfg {
   static constexpr int kChunks = kColsPerWarp / 32;  // 32-column chunks per epilogue warp
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
-  static_assert(!SIDE || (FP4 && BN == 256 && offSide % 1024 == 0 && kSide >= 4 * kBM * 128), "side tile");
+  static_assert(!SIDE || (FP4 && BN == 256 && PAIR && offSide % 1024 == 0), "side tile");
 };
 
 // Tile t -> (m_blk, n_blk).  Tiles run in bands of m_group m-blocks: inside a band the
@@ -157,7 +161,7 @@ __device__ __forceinline__ int stg_off(int r, int j) { return r * 64 + ((j ^ ((r
 
 // One CTA per SM (persistent).  10 warps spread over the SM's 4 sub-partitions put 3 warps on
 // two of them, so a thread gets at most 168 of a sub-partition's 16 K registers.
-template <int BN, int STAGES, bool FP4, bool PAIR, bool SIDE>
+template <int BN, int STAGES, bool FP4, bool PAIR, int SIDE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!SIDE || tile >= t_end) return -1;
     int mb, nb;
     tile_coords(tile, p, mb, nb);
-    if (p.rope_cos) return nb * BN < p.hn_cols ? mb : -1;
+    if (SIDE == 1) return nb * BN < p.hn_cols ? mb : -1;
     return tile;
   };
   // wait limit of this CTA: the default, or the armed test's short one in the first CTA (pair)
@@ -441,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // cp.async copies, half a warp per 256-byte row (positions wrap at rope_S inside a tile;
     // rows past M are skipped), or the residual tile by four TMA boxes (rows past M read as
     // zeros).
-    const bool side_rope = p.rope_cos != nullptr;
+    constexpr bool side_rope = SIDE == 1;
     uint8_t* side = smem + C::offSide;
     uint32_t sit = 0;  // side tiles issued
     int loaded = -1;   // key of the side tile in shared memory (-1: released)
@@ -470,8 +474,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(side_full);
       } else if (lane == 0) {
-        mbar_arrive_expect_tx(side_full, 4u * kBM * 128u);
+        // gate rows of this CTA's rows inside M (gate_rows >= 128: one or two)
+        const int g0 = m0 / (int)p.gate_rows;
+        const int ng = (p.gate && m0 < p.M) ? (min(m0 + kBM, p.M) - 1) / (int)p.gate_rows - g0 + 1 : 0;
+        mbar_arrive_expect_tx(side_full, 4u * kBM * 128u + (uint32_t)ng * (BN * 2));
         for (int b = 0; b < 4; ++b) tma_load_2d(side + b * (kBM * 128), &tmR, side_full, n0 + 64 * b, m0);
+        for (int i = 0; i < ng; ++i)
+          bulk_load(side + C::kSideGate + i * (BN * 2), p.gate + (int64_t)(g0 + i) * p.ld_gate + n0, BN * 2, side_full);
       }
       __syncwarp();
       ++sit;
@@ -496,8 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t out_policy = l2_policy_evict_first();
     uint32_t it = 0, nstore = 0;
     // SIDE kernels: the rotary tables (head norm + RoPE) or the residual come from the side tile
-    const bool side_rope = SIDE && p.rope_cos != nullptr;
-    const bool side_res = SIDE && !side_rope;
+    constexpr bool side_rope = SIDE == 1;
+    constexpr bool side_res = SIDE == 2;
     const uint32_t side = smem_u32(smem + C::offSide);
     uint32_t sit = 0;  // side tiles released
     int cur = -1;      // key of the side tile this warp has seen land (-1: none)
@@ -677,81 +686,126 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
       }
+      if constexpr (SIDE == 2) {
+        // out = bf16(residual + bf16(y * gate)) written over the lane's own residual chunks in
+        // the side tile and stored from there, one 32-row x 64-column TMA box (the 128-byte
+        // swizzle it was loaded with) per two chunks; the gate from its segments in the tile
+        const bool gated = p.gate != nullptr;
+        const int gsel = gated ? max(0, (int)(min(row, (int64_t)p.M - 1) / p.gate_rows - m0 / p.gate_rows)) : 0;
+        const uint32_t gb = side + C::kSideGate + gsel * (BN * 2) + half * (C::kColsPerWarp * 2);
 #pragma unroll
-      for (int c = 0; c < C::kChunks; ++c) {
-        if (sm && c >= 2) break;  // SwiGLU: two 32-column output chunks per warp
-        if (c + 1 < C::kChunks) {  // the next chunk's gate / residual segments into L1
-          if (gate_row) prefetch_l1(gate_row + (c + 1) * 32);
-          if (res_row) prefetch_l1(res_row + (c + 1) * 32);
-        }
-        const int ncol = sm ? (n0 >> 1) + half * 64 + c * 32 : ncol0 + c * 32;
-        // FP4 tiles never cross N (N % BN == 0); the bf16 GEMM's last tile can (rank < BN)
-        if (!FP4 && ncol >= p.N) break;
-        if (FP4) {
-          if (gate_row) {  // y = bf16(y * gate), as the reference's eager `y * gate`
-            uint4 gx[4];
-            ld_global_row64(gate_row + c * 32, gx);
+        for (int bb = 0; bb < C::kChunks / 2; ++bb) {
+          const int b = half * 2 + bb;  // 64-column box of the side tile
+          const uint32_t rb = side + b * (kBM * 128) + srow * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t gw[4] = {gx[j].x, gx[j].y, gx[j].z, gx[j].w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) y[c][4 * j + i] = mul_bf2(y[c][4 * j + i], gw[i]);
-            }
-          }
-          if (res_row || side_res) {  // out = bf16(residual + y)
-            uint4 rx[4];
-            if (side_res) {  // box half * 2 + c / 2, 16-byte chunk k of the row at k ^ (row & 7)
-              const uint32_t rb = side + (half * 2 + (c >> 1)) * (kBM * 128) + srow * 128;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) rx[j] = ld_shared_v4(rb + ((((c & 1) * 4 + j) ^ (srow & 7)) << 4));
-            } else {
-              ld_global_row64(res_row + c * 32, rx);
-            }
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * bb + cc;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
+              const uint32_t adr = rb + (((cc * 4 + j) ^ (srow & 7)) << 4);
+              const uint4 rx = ld_shared_v4(adr);
+              const uint32_t rw[4] = {rx.x, rx.y, rx.z, rx.w};
+              const uint4 g4 = gated ? ld_shared_v4(gb + c * 64 + j * 16) : make_uint4(0, 0, 0, 0);
+              const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+              uint32_t o[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(y[c][4 * j + i])));
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t v = gated ? mul_bf2(y[c][4 * j + i], gw[i]) : y[c][4 * j + i];
+                o[i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(v)));
+              }
+              st_shared_v4(adr, o[0], o[1], o[2], o[3]);
             }
           }
-          // 32 rows x 32 columns, 64-byte swizzle (conflict-free), written by one TMA store;
-          // two buffers per warp: wait only until the store before last has read its source
-          const uint32_t buf = stg + (nstore & 1u) * 2048u;
-          if (nstore >= 2) {
-            if (lane == 0) bulk_wait_read<1>();
-            __syncwarp();
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            st_shared_v4(buf + stg_off(lane, j), y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2], y[c][4 * j + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {  // rows >= M are clipped by the tensor map
+            const uint32_t src = side + b * (kBM * 128) + q * 32 * 128;
             if (p.out_evict_first)
-              tma_store_2d_s_hint(&tmO, buf, ncol, m0 + q * 32, out_policy);
+              tma_store_2d_s_hint(&tmO, src, n0 + 64 * b, m0 + q * 32, out_policy);
             else
-              tma_store_2d_s(&tmO, buf, ncol, m0 + q * 32);
+              tma_store_2d_s(&tmO, src, n0 + 64 * b, m0 + q * 32);
             bulk_commit();
           }
-          ++nstore;
-        } else {
-          // bf16 GEMM (LoRA down-projection, narrow outputs): transpose through shared
-          // memory so each store instruction writes 8 rows x 64 contiguous bytes
+        }
+        if (lane == 0) bulk_wait_read<0>();  // the stores have read the side tile
+        __syncwarp();
+      } else {
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            st_shared_v4(stg + lane * kStgPitch + j * 16, y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2],
-                         y[c][4 * j + 3]);
-          __syncwarp();
-          const int trow = lane >> 2, tgr = lane & 3;
-#pragma unroll
-          for (int sp = 0; sp < 4; ++sp) {
-            const int rl = trow + 8 * sp;
-            const int64_t grow = (int64_t)m0 + q * 32 + rl;
-            const uint4 o = ld_shared_v4(stg + rl * kStgPitch + tgr * 16);
-            const int cc = ncol + tgr * 8;
-            if (grow < p.M && cc < p.N) st_global_v4(p.out + grow * p.ldo + cc, o);
+        for (int c = 0; c < C::kChunks; ++c) {
+          if (sm && c >= 2) break;  // SwiGLU: two 32-column output chunks per warp
+          if (c + 1 < C::kChunks) {  // the next chunk's gate / residual segments into L1
+            if (gate_row) prefetch_l1(gate_row + (c + 1) * 32);
+            if (res_row) prefetch_l1(res_row + (c + 1) * 32);
           }
-          __syncwarp();
+          const int ncol = sm ? (n0 >> 1) + half * 64 + c * 32 : ncol0 + c * 32;
+          // FP4 tiles never cross N (N % BN == 0); the bf16 GEMM's last tile can (rank < BN)
+          if (!FP4 && ncol >= p.N) break;
+          if (FP4) {
+            if (gate_row) {  // y = bf16(y * gate), as the reference's eager `y * gate`
+              uint4 gx[4];
+              ld_global_row64(gate_row + c * 32, gx);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t gw[4] = {gx[j].x, gx[j].y, gx[j].z, gx[j].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) y[c][4 * j + i] = mul_bf2(y[c][4 * j + i], gw[i]);
+              }
+            }
+            if (res_row || side_res) {  // out = bf16(residual + y)
+              uint4 rx[4];
+              if (side_res) {  // box half * 2 + c / 2, 16-byte chunk k of the row at k ^ (row & 7)
+                const uint32_t rb = side + (half * 2 + (c >> 1)) * (kBM * 128) + srow * 128;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) rx[j] = ld_shared_v4(rb + ((((c & 1) * 4 + j) ^ (srow & 7)) << 4));
+              } else {
+                ld_global_row64(res_row + c * 32, rx);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(y[c][4 * j + i])));
+              }
+            }
+            // 32 rows x 32 columns, 64-byte swizzle (conflict-free), written by one TMA store;
+            // two buffers per warp: wait only until the store before last has read its source
+            const uint32_t buf = stg + (nstore & 1u) * 2048u;
+            if (nstore >= 2) {
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(buf + stg_off(lane, j), y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2], y[c][4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {  // rows >= M are clipped by the tensor map
+              if (p.out_evict_first)
+                tma_store_2d_s_hint(&tmO, buf, ncol, m0 + q * 32, out_policy);
+              else
+                tma_store_2d_s(&tmO, buf, ncol, m0 + q * 32);
+              bulk_commit();
+            }
+            ++nstore;
+          } else {
+            // bf16 GEMM (LoRA down-projection, narrow outputs): transpose through shared
+            // memory so each store instruction writes 8 rows x 64 contiguous bytes
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(stg + lane * kStgPitch + j * 16, y[c][4 * j], y[c][4 * j + 1], y[c][4 * j + 2],
+                           y[c][4 * j + 3]);
+            __syncwarp();
+            const int trow = lane >> 2, tgr = lane & 3;
+#pragma unroll
+            for (int sp = 0; sp < 4; ++sp) {
+              const int rl = trow + 8 * sp;
+              const int64_t grow = (int64_t)m0 + q * 32 + rl;
+              const uint4 o = ld_shared_v4(stg + rl * kStgPitch + tgr * 16);
+              const int cc = ncol + tgr * 8;
+              if (grow < p.M && cc < p.N) st_global_v4(p.out + grow * p.ldo + cc, o);
+            }
+            __syncwarp();
+          }
         }
       }
       if (need_side && side_key(tile + t_step) != skey) {  // end of the run: release the side tile
@@ -781,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 constexpr int kBandMBlocks = 8;
 
-template <int BN, int STAGES, bool FP4, bool PAIR = false, bool SIDE = false>
+template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& la, const CUtensorMap& lb,
                 const CUtensorMap& o, GemmParams p, cudaStream_t st, const CUtensorMap* sfa = nullptr,
                 const CUtensorMap* sfb = nullptr, const CUtensorMap* res = nullptr) {
@@ -812,7 +866,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   // large-M launches sweep N in bands of 8 m-blocks; smaller ones keep m-fastest order
   const double a_bytes = (double)p.M * p.K * (FP4 ? 0.5625 : 2.0);
   p.m_group = (a_bytes > 24e6) ? std::min(p.m_tiles, kBandMBlocks) : p.m_tiles;
-  if (SIDE && p.rope_cos) {
+  if (SIDE == 1) {
     // each pair sweeps N over its own m-blocks (contiguous tiles, n fastest): the rotary
     // tables of an m-block are loaded once for all its head tiles; the pairs' A blocks
     // (256 KB each) stay in L2 while they are swept
@@ -1014,19 +1068,22 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
     t_stall_wait_ns = 0;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // A side tile (three stages instead of four, for its 68 KB of shared memory) when the
-  // epilogue would otherwise read per-row operands one row per lane: the rotary tables of
-  // the head-norm + RoPE epilogue, or the residual (gemm_check: never both, never with
-  // SwiGLU; residual rows 16-byte aligned)
+  // A side tile when the epilogue would otherwise read per-row operands one row per lane
+  // (gemm_check: never both, never with SwiGLU; residual rows 16-byte aligned): the rotary
+  // tables of the head-norm + RoPE epilogue (68 KB: three stages), or the residual, which the
+  // output overwrites and is stored from (no staging buffers: four stages, 64 x 32 store
+  // boxes), with the gate rows when each spans at least a tile's 128 rows
   const bool side_rope = a->rope_cos && a->hn_cols > 0;
-  const bool side_res = a->residual != nullptr;
-  if (pair && side_stage_enabled() && (side_rope || side_res)) {
-    CUtensorMap tr;
-    memset(&tr, 0, sizeof tr);
-    if (side_res)
-      DEMON_RC(make_tmap_2d(&tr, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
-                            (uint64_t)a->ldr * 2, 64, 128));
-    return launch_gemm<256, 3, true, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb, &tr);
+  const bool side_res = a->residual != nullptr && (!a->gate || a->gate_rows >= 128);
+  if (pair && side_stage_enabled() && side_rope)
+    return launch_gemm<256, 3, true, true, 1>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
+  if (pair && side_stage_enabled() && side_res) {
+    CUtensorMap tr, to2;
+    DEMON_RC(make_tmap_2d(&tr, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,
+                          (uint64_t)a->ldr * 2, 64, 128));
+    DEMON_RC(make_tmap_2d(&to2, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)n_out, (uint64_t)M,
+                          (uint64_t)a->ldo * 2, 64, 32));
+    return launch_gemm<256, 4, true, true, 2>(ta, tb, tla, tlb, to2, p, st, &tsfa, &tsfb, &tr);
   }
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);

@@ -205,8 +205,10 @@ wq = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
 wk = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
 cos = torch.randn(S, 128, generator=g, device=dev).to(torch.bfloat16)
 sin = torch.randn(S, 128, generator=g, device=dev).to(torch.bfloat16)
+gate150 = torch.randn(M // 150 + 1, 768, generator=g, device=dev).to(torch.bfloat16)
 out = {
     "res": Q.gemm(a, w1, residual=res, gate=gate, gate_rows=7),
+    "res_gate150": Q.gemm(a, w1, residual=res, gate=gate150, gate_rows=150),
     "res_plain": Q.gemm(a, w1, residual=res),
     "rope": Q.gemm(a, wqkv, head_norm=((hq + hk) * 128, hq * 128, wq, wk, 1e-6), rope=(cos, sin, S)),
 }
@@ -215,10 +217,12 @@ torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[2])
 
 
 def test_side_tile_matches_direct_path(cuda, tmp_path):
-    """The epilogue's side tile (rotary rows by cp.async, residual by TMA boxes, three
-    pipeline stages) and the direct per-lane reads (DEMON_GEMM_SIDE=0, four stages) give the
-    same bits: a strided residual with a per-7-rows gate, and head norm + RoPE whose positions
-    wrap inside tiles, at an M that leaves the last CTA pair partly empty."""
+    """The epilogue's side tile (rotary rows by cp.async; the residual by TMA boxes with the
+    gate rows, the output stored from the tile) and the direct per-lane reads
+    (DEMON_GEMM_SIDE=0) give the same bits: a strided residual alone, with a gate per 150 rows
+    (tiles that straddle two gate rows) and with a gate per 7 rows (the direct path in both
+    runs), and head norm + RoPE whose positions wrap inside tiles, at an M that leaves the
+    last CTA pair partly empty."""
     import os
     import subprocess
     import sys
