@@ -1377,7 +1377,12 @@ def run_kernel_workload(args):
     number, else 12000; the tick's is 96000);
     ``attention``: the DiT's band (window 128), global and cross attention over ``--seqs``
     sequences of 750 tokens (GQA 16/8 x 128, text 256), with ``--vs-cudnn`` also the cuDNN
-    kernels on the same inputs.  Prints per-launch times."""
+    kernels on the same inputs;
+    ``layer``: the six NVFP4 GEMMs of a DiT layer at M rows (``--shape`` when it is one number,
+    else 96000: the tick's) with their epilogues -- q/k/v with head norm + RoPE, o_proj and down
+    with the AdaLN gate (one row per 750 tokens) and the residual, the cross-attention q with
+    head norm, the cross-attention o with the residual, gate/up with SwiGLU -- each beside the
+    same operands without the epilogue.  Prints per-launch times."""
     import torch
     from demon_b200 import _build, _native as nat, nvfp4
     _build.build()
@@ -1400,6 +1405,41 @@ def run_kernel_workload(args):
                 launches.append((f"cublaslt {M}x{N}x{K}", 2.0 * M * N * K,
                                  lambda fa=fa, fb=fb, sa=sa, sb=sb: torch._scaled_mm(
                                      fa, fb, sa, sb, out_dtype=torch.bfloat16)))
+    elif args.workload == "layer":
+        M, S = (int(args.shape) if args.shape.isdigit() else 96000), 750
+        hq, hk = 16, 8
+
+        def wt(n, k):
+            return nvfp4.pack_weight((torch.randn(n, k, generator=g, device=dev) * 0.03).to(torch.bfloat16))
+        a2 = nvfp4.quantize(torch.randn(M, 2048, generator=g, device=dev).to(torch.bfloat16))
+        a6 = nvfp4.quantize(torch.randn(M, 6144, generator=g, device=dev).to(torch.bfloat16))
+        wqkv, wo, wd = wt((hq + 2 * hk) * 128, 2048), wt(2048, 2048), wt(2048, 6144)
+        wu = nvfp4.interleave_weights(wt(6144, 2048), wt(6144, 2048))
+        res = torch.randn(M, 2048, generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn((M + S - 1) // S, 2048, generator=g, device=dev).to(torch.bfloat16)
+        nw = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+        pos = torch.arange(S, dtype=torch.float32, device=dev)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev).float() / 128))
+        emb = torch.cat([pos[:, None] * inv[None]] * 2, -1)
+        rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16), S)
+        o4, o2 = (torch.empty(M, n, dtype=torch.bfloat16, device=dev) for n in (4096, 2048))
+        o6 = torch.empty(M, 6144, dtype=torch.bfloat16, device=dev)
+        hn_qkv, hn_q = ((hq + hk) * 128, hq * 128, nw, nw, 1e-6), (2048, 2048, nw, None, 1e-6)
+        f = 2.0 * M * 2048
+        launches += [
+            ("qkv head_norm+rope", f * 4096, lambda: nvfp4.gemm(a2, wqkv, head_norm=hn_qkv, rope=rope, out=o4)),
+            ("qkv plain", f * 4096, lambda: nvfp4.gemm(a2, wqkv, out=o4)),
+            ("o_proj gate+residual", f * 2048,
+             lambda: nvfp4.gemm(a2, wo, residual=res, gate=gate, gate_rows=S, out=o2)),
+            ("o_proj plain", f * 2048, lambda: nvfp4.gemm(a2, wo, out=o2)),
+            ("cross_q head_norm", f * 2048, lambda: nvfp4.gemm(a2, wo, head_norm=hn_q, out=o2)),
+            ("cross_o residual", f * 2048, lambda: nvfp4.gemm(a2, wo, residual=res, out=o2)),
+            ("gate_up swiglu", f * 12288, lambda: nvfp4.gemm(a2, wu, silu_mul=True, out=o6)),
+            ("gate_up plain", f * 12288, lambda: nvfp4.gemm(a2, wu)),
+            ("down gate+residual", f * 6144,
+             lambda: nvfp4.gemm(a6, wd, residual=res, gate=gate, gate_rows=S, out=o2)),
+            ("down plain", f * 6144, lambda: nvfp4.gemm(a6, wd, out=o2)),
+        ]
     elif args.workload == "attention":
         from demon_b200.attention import attention
         B, S, L, hq, hk, D = args.seqs, 750, L5, 16, 8, 128
@@ -1461,7 +1501,7 @@ def run_kernel_workload(args):
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.steps
-        flops = args.workload in ("gemm", "attention")
+        flops = args.workload in ("gemm", "attention", "layer")
         unit = "TFLOP/s" if flops else "GB/s"
         res[name] = {"us": us, unit: work / (us * 1e-6) / (1e12 if flops else 1e9)}
     print(json.dumps({"workload": args.workload, "shape": args.shape, "steps": args.steps, "kernels": res,
@@ -1474,7 +1514,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows", "attention"])
+    ap.add_argument("--workload", default="stream", choices=["stream", "linear", "gemm", "rows", "attention", "layer"])
     ap.add_argument("--seqs", type=int, default=128, help="sequences of 750 tokens for --workload attention")
     ap.add_argument("--vs-cudnn", action="store_true",
                     help="with --workload attention: also time the cuDNN attention kernels on the same inputs")
@@ -1494,7 +1534,7 @@ def main():
     if args.impl == "reference":
         (run_reference_stream if args.workload == "stream" else run_reference)(args)
         return
-    if args.workload in ("gemm", "rows", "attention"):
+    if args.workload in ("gemm", "rows", "attention", "layer"):
         run_kernel_workload(args)
         return
     (run_stream if args.workload == "stream" else run_linear)(args)
