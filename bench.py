@@ -1415,7 +1415,7 @@ def run_kernel_workload(args):
         a6 = nvfp4.quantize(torch.randn(M, 6144, generator=g, device=dev).to(torch.bfloat16))
         wqkv, wo, wd = wt((hq + 2 * hk) * 128, 2048), wt(2048, 2048), wt(2048, 6144)
         wu = nvfp4.interleave_weights(wt(6144, 2048), wt(6144, 2048))
-        res = torch.randn(M, 2048, generator=g, device=dev).to(torch.bfloat16)
+        resid = torch.randn(M, 2048, generator=g, device=dev).to(torch.bfloat16)
         gate = torch.randn((M + S - 1) // S, 2048, generator=g, device=dev).to(torch.bfloat16)
         nw = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
         pos = torch.arange(S, dtype=torch.float32, device=dev)
@@ -1424,21 +1424,22 @@ def run_kernel_workload(args):
         rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16), S)
         o4, o2 = (torch.empty(M, n, dtype=torch.bfloat16, device=dev) for n in (4096, 2048))
         o6 = torch.empty(M, 6144, dtype=torch.bfloat16, device=dev)
+        o12 = torch.empty(M, 12288, dtype=torch.bfloat16, device=dev)
         hn_qkv, hn_q = ((hq + hk) * 128, hq * 128, nw, nw, 1e-6), (2048, 2048, nw, None, 1e-6)
-        f = 2.0 * M * 2048
+        fl = 2.0 * M * 2048
         launches += [
-            ("qkv head_norm+rope", f * 4096, lambda: nvfp4.gemm(a2, wqkv, head_norm=hn_qkv, rope=rope, out=o4)),
-            ("qkv plain", f * 4096, lambda: nvfp4.gemm(a2, wqkv, out=o4)),
-            ("o_proj gate+residual", f * 2048,
-             lambda: nvfp4.gemm(a2, wo, residual=res, gate=gate, gate_rows=S, out=o2)),
-            ("o_proj plain", f * 2048, lambda: nvfp4.gemm(a2, wo, out=o2)),
-            ("cross_q head_norm", f * 2048, lambda: nvfp4.gemm(a2, wo, head_norm=hn_q, out=o2)),
-            ("cross_o residual", f * 2048, lambda: nvfp4.gemm(a2, wo, residual=res, out=o2)),
-            ("gate_up swiglu", f * 12288, lambda: nvfp4.gemm(a2, wu, silu_mul=True, out=o6)),
-            ("gate_up plain", f * 12288, lambda: nvfp4.gemm(a2, wu)),
-            ("down gate+residual", f * 6144,
-             lambda: nvfp4.gemm(a6, wd, residual=res, gate=gate, gate_rows=S, out=o2)),
-            ("down plain", f * 6144, lambda: nvfp4.gemm(a6, wd, out=o2)),
+            ("qkv head_norm+rope", fl * 4096, lambda: nvfp4.gemm(a2, wqkv, head_norm=hn_qkv, rope=rope, out=o4)),
+            ("qkv plain", fl * 4096, lambda: nvfp4.gemm(a2, wqkv, out=o4)),
+            ("o_proj gate+residual", fl * 2048,
+             lambda: nvfp4.gemm(a2, wo, residual=resid, gate=gate, gate_rows=S, out=o2)),
+            ("o_proj plain", fl * 2048, lambda: nvfp4.gemm(a2, wo, out=o2)),
+            ("cross_q head_norm", fl * 2048, lambda: nvfp4.gemm(a2, wo, head_norm=hn_q, out=o2)),
+            ("cross_o residual", fl * 2048, lambda: nvfp4.gemm(a2, wo, residual=resid, out=o2)),
+            ("gate_up swiglu", fl * 12288, lambda: nvfp4.gemm(a2, wu, silu_mul=True, out=o6)),
+            ("gate_up plain", fl * 12288, lambda: nvfp4.gemm(a2, wu, out=o12)),
+            ("down gate+residual", fl * 6144,
+             lambda: nvfp4.gemm(a6, wd, residual=resid, gate=gate, gate_rows=S, out=o2)),
+            ("down plain", fl * 6144, lambda: nvfp4.gemm(a6, wd, out=o2)),
         ]
     elif args.workload == "attention":
         from demon_b200.attention import attention

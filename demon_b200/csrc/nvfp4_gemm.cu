@@ -92,9 +92,12 @@ static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads *
               "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
-// SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual
+// SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual, 3 none and
+// no per-column vector either (no bias, no head norm: the space goes to a fifth stage)
 template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 struct GemmCfg {
+  static constexpr bool kSideTile = SIDE == 1 || SIDE == 2;
+  static constexpr bool kColVec = SIDE != 3;  // bias / column scale staged per warp
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
   static constexpr int kSFA = FP4 ? 2048 : 0;
@@ -117,9 +120,9 @@ struct GemmCfg {
   static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 : 0;
   static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
   static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
-  static constexpr int offHn = offCol + kEpiWarps * (BN / 2) * 4;  // fp32 head-norm weight per warp
-  static constexpr int offBar = offHn + (FP4 && SIDE != 2 ? kEpiWarps * (BN / 2) * 4 : 0);
-  static constexpr int kBars = 2 * STAGES + 3 + (SIDE ? 2 : 0);
+  static constexpr int offHn = offCol + (kColVec ? kEpiWarps * (BN / 2) * 4 : 0);  // head-norm weight per warp
+  static constexpr int offBar = offHn + (FP4 && SIDE != 2 && SIDE != 3 ? kEpiWarps * (BN / 2) * 4 : 0);
+  static constexpr int kBars = 2 * STAGES + 3 + (kSideTile ? 2 : 0);
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
   static constexpr int kSfaCol = BN;                 // 4 columns per K=64 step, 4 steps
@@ -176,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* mma_done = acc_empty + 1;
-  uint64_t* side_full = mma_done + 1;   // SIDE kernels only
+  uint64_t* side_full = mma_done + 1;   // side-tile kernels only
   uint64_t* side_empty = mma_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::offMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::offMisc + 4);
@@ -197,11 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_begin = p.tile_chunk ? cid * p.tile_chunk : cid;
   const int t_step = p.tile_chunk ? 1 : ncl;
   const int t_end = p.tile_chunk ? min(num_tiles, t_begin + p.tile_chunk) : num_tiles;
-  // SIDE kernels: the side tile a tile reads, as a key (-1: none).  The rotary tables depend
+  // Side-tile kernels: the side tile a tile reads, as a key (-1: none).  The rotary tables depend
   // on the rows only, so consecutive tiles of one m-block share one load; a residual tile is
   // its own.  A side tile is released after the last of a run of tiles with its key.
   auto side_key = [&](int tile) -> int {
-    if (!SIDE || tile >= t_end) return -1;
+    if (!C::kSideTile || tile >= t_end) return -1;
     int mb, nb;
     tile_coords(tile, p, mb, nb);
     if (SIDE == 1) return nb * BN < p.hn_cols ? mb : -1;
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);  // the pair's epilogue warps
     mbar_init(mma_done, 1);
-    if (SIDE) {
+    if (C::kSideTile) {
       mbar_init(side_full, 1);
       mbar_init(side_empty, kEpiWarps);  // this CTA's epilogue warps
     }
@@ -438,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, &never, globaltimer(), p.status, 9, lim);
     }
     __syncwarp();
-   } else if (SIDE && warp == 2) {
+   } else if (C::kSideTile && warp == 2) {
     // ------------------------------------------------------------ side-input loader
     // At the first tile of each run of tiles with one side key, once the epilogue warps have
     // released the previous side tile: the table rows of the m-block by coalesced 16-byte
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     const uint64_t out_policy = l2_policy_evict_first();
     uint32_t it = 0, nstore = 0;
-    // SIDE kernels: the rotary tables (head norm + RoPE) or the residual come from the side tile
+    // side-tile kernels: the rotary tables (head norm + RoPE) or the residual come from the side tile
     constexpr bool side_rope = SIDE == 1;
     constexpr bool side_res = SIDE == 2;
     const uint32_t side = smem_u32(smem + C::offSide);
@@ -523,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Everything that does not depend on the accumulator is fetched while the MMAs run:
       // the per-column vector (bias, or the bf16 GEMM's column scale) into shared memory,
       // the lane's row scale, and L2 prefetches of its gate / residual row segments.
-      for (int i = lane; i < C::kColsPerWarp; i += 32) {
+      for (int i = lane; C::kColVec && i < C::kColsPerWarp; i += 32) {
         const int n = sm ? n0 + (i < 64 ? half * 64 + i : 128 + half * 64 + (i - 64)) : ncol0 + i;
         float cv = 0.0f;
         if (n < p.N)
@@ -584,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < C::kChunks; ++c) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 cv = ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j));
+          const float4 cv = C::kColVec ? ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
           if (FP4) {
             const float ac = (sm && c >= 2) ? alpha_u : alpha;
             const float2 al = make_float2(ac, ac);
@@ -1085,6 +1088,10 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                           (uint64_t)a->ldo * 2, 64, 32));
     return launch_gemm<256, 4, true, true, 2>(ta, tb, tla, tlb, to2, p, st, &tsfa, &tsfb, &tr);
   }
+  // no bias, head norm or residual: no per-column vector, and its shared memory buys a fifth
+  // stage (the SwiGLU gate/up GEMM: 1190 -> 985 us at M = 96,000)
+  if (pair && !a->bias && a->hn_cols == 0)
+    return launch_gemm<256, 5, true, true, 3>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
   return launch_gemm<128, 5, true>(ta, tb, tla, tlb, to, p, st);
