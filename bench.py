@@ -1382,7 +1382,8 @@ def run_kernel_workload(args):
     else 96000: the tick's) with their epilogues -- q/k/v with head norm + RoPE, o_proj and down
     with the AdaLN gate (one row per 750 tokens) and the residual, the cross-attention q with
     head norm, the cross-attention o with the residual, gate/up with SwiGLU -- each beside the
-    same operands without the epilogue.  Prints per-launch times."""
+    same operands without the epilogue, ``--steps`` launches of each replayed from a CUDA graph.
+    Prints per-launch times."""
     import torch
     from demon_b200 import _build, _native as nat, nvfp4
     _build.build()
@@ -1496,10 +1497,21 @@ def run_kernel_workload(args):
     res = {}
     for name, work, f in launches:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            f()
-        e1.record()
+        if args.workload == "layer":  # replayed from a CUDA graph: no host work between launches
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(args.steps):
+                    f()
+            gr.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            gr.replay()
+            e1.record()
+        else:
+            e0.record()
+            for _ in range(args.steps):
+                f()
+            e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.steps
         flops = args.workload in ("gemm", "attention", "layer")
