@@ -546,8 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float a_row = (row_ok && p.a_gs) ? p.a_gs[p.a_gs_per_row ? row : 0] : 0.0f;
       const float alpha = (row_ok && p.a_gs) ? a_row * p.w_gs[p.w_gs_per_block ? wblk : 0] : 0.0f;
       const float alpha_u = sm ? a_row * p.w_gs[p.w_gs_per_block ? wblk + 1 : 0] : alpha;
-      const __nv_bfloat16* gate_row =
-          (FP4 && p.gate && row_ok) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
+      const __nv_bfloat16* gate_row =  // (the residual side tile carries the gate rows itself)
+          (FP4 && p.gate && row_ok && !side_res) ? p.gate + (row / p.gate_rows) * p.ld_gate + ncol0 : nullptr;
       const __nv_bfloat16* res_row =
           (FP4 && p.residual && row_ok && !side_res) ? p.residual + row * p.ldr + ncol0 : nullptr;
 #pragma unroll
@@ -694,29 +694,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the side tile and stored from there, one 32-row x 64-column TMA box (the 128-byte
         // swizzle it was loaded with) per two chunks; the gate from its segments in the tile
         const bool gated = p.gate != nullptr;
-        const int gsel = gated ? max(0, (int)(min(row, (int64_t)p.M - 1) / p.gate_rows - m0 / p.gate_rows)) : 0;
+        // the lane's gate row: the tile's first or second (a gate row spans >= 128 rows)
+        const int gr = gated ? (int)p.gate_rows : 1;
+        const int gnext = (m0 / gr + 1) * gr;  // first row of the second gate row (warp-uniform)
+        const int gsel = (gated && (int)min(row, (int64_t)p.M - 1) >= gnext) ? 1 : 0;
         const uint32_t gb = side + C::kSideGate + gsel * (BN * 2) + half * (C::kColsPerWarp * 2);
 #pragma unroll
         for (int bb = 0; bb < C::kChunks / 2; ++bb) {
           const int b = half * 2 + bb;  // 64-column box of the side tile
           const uint32_t rb = side + b * (kBM * 128) + srow * 128;
+          // every shared-memory read of the box first (the in-place stores below would order
+          // each read after the previous store), then the arithmetic and the stores
+          uint4 rx[2][4], g4[2][4];
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              rx[cc][j] = ld_shared_v4(rb + (((cc * 4 + j) ^ (srow & 7)) << 4));
+              g4[cc][j] = gated ? ld_shared_v4(gb + (2 * bb + cc) * 64 + j * 16) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const int c = 2 * bb + cc;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t adr = rb + (((cc * 4 + j) ^ (srow & 7)) << 4);
-              const uint4 rx = ld_shared_v4(adr);
-              const uint32_t rw[4] = {rx.x, rx.y, rx.z, rx.w};
-              const uint4 g4 = gated ? ld_shared_v4(gb + c * 64 + j * 16) : make_uint4(0, 0, 0, 0);
-              const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+              const uint32_t rw[4] = {rx[cc][j].x, rx[cc][j].y, rx[cc][j].z, rx[cc][j].w};
+              const uint32_t gw[4] = {g4[cc][j].x, g4[cc][j].y, g4[cc][j].z, g4[cc][j].w};
               uint32_t o[4];
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const uint32_t v = gated ? mul_bf2(y[c][4 * j + i], gw[i]) : y[c][4 * j + i];
                 o[i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(v)));
               }
-              st_shared_v4(adr, o[0], o[1], o[2], o[3]);
+              st_shared_v4(rb + (((cc * 4 + j) ^ (srow & 7)) << 4), o[0], o[1], o[2], o[3]);
             }
           }
           fence_proxy_async_smem();
