@@ -683,8 +683,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const uint32_t a = y[c][4 * j + i], b = y[c + 2][4 * j + i];
-                y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(mul_bf2(a, cw1[i])), bf2_f2(mul_bf2(b ^ 0x80008000u, sw1[i]))));
-                y[c + 2][4 * j + i] = f2_bf2(add_f2(bf2_f2(mul_bf2(b, cw2[i])), bf2_f2(mul_bf2(a, sw2[i]))));
+                // each product and the sum rounded to bf16 once (add_bf2: the exact sum of two
+                // bf16 values rounded once equals the fp32 sum rounded to bf16)
+                y[c][4 * j + i] = add_bf2(mul_bf2(a, cw1[i]), mul_bf2(b ^ 0x80008000u, sw1[i]));
+                y[c + 2][4 * j + i] = add_bf2(mul_bf2(b, cw2[i]), mul_bf2(a, sw2[i]));
               }
             }
         }
@@ -724,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const uint32_t v = gated ? mul_bf2(y[c][4 * j + i], gw[i]) : y[c][4 * j + i];
-                o[i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(v)));
+                o[i] = add_bf2(rw[i], v);  // bf16(residual + y), as the fp32 sum rounded to bf16
               }
               st_shared_v4(rb + (((cc * 4 + j) ^ (srow & 7)) << 4), o[0], o[1], o[2], o[3]);
             }
@@ -777,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 4; ++j) {
                 const uint32_t rw[4] = {rx[j].x, rx[j].y, rx[j].z, rx[j].w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) y[c][4 * j + i] = f2_bf2(add_f2(bf2_f2(rw[i]), bf2_f2(y[c][4 * j + i])));
+                for (int i = 0; i < 4; ++i) y[c][4 * j + i] = add_bf2(rw[i], y[c][4 * j + i]);
               }
             }
             // 32 rows x 32 columns, 64-byte swizzle (conflict-free), written by one TMA store;
