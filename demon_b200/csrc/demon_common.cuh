@@ -506,6 +506,15 @@ __device__ __forceinline__ uint32_t mul_bf2(uint32_t a, uint32_t b) {
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// se += lo(w)^2 and so += hi(w)^2 for the two bf16 halves of w, by the mixed-precision FMA
+// (bf16 x bf16 + fp32 -> fp32, one rounding): the bf16 product is exact in fp32, so each step
+// equals the fp32 FMA of the widened values.
+__device__ __forceinline__ void sq_acc_bf2(uint32_t w, float& se, float& so) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, lo, lo, %0;\n\tfma.rn.f32.bf16 %1, hi, hi, %1;\n\t}"
+      : "+f"(se), "+f"(so)
+      : "r"(w));
+}
 // bf16(a + b) per half (single rounding of the exact sum; equal to the fp32 sum rounded to bf16).
 __device__ __forceinline__ uint32_t add_bf2(uint32_t a, uint32_t b) {
   uint32_t r;

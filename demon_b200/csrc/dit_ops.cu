@@ -71,18 +71,13 @@ __device__ __forceinline__ uint4 norm8(uint4 x, uint4 w, uint4 s1, uint4 sh, flo
 }
 
 // Sum of squares of eight bf16 values onto acc: even elements in one fp32 chain, odd ones in
-// another, summed at the end.  The mixed-precision FMA (bf16 x bf16 + fp32 -> fp32, one rounding)
-// takes the bf16 halves directly; the bf16 product is exact in fp32, so each step equals the
-// fp32 FMA of the widened values.
+// another, summed at the end (sq_acc_bf2: the same bits as widening first).
 __device__ __forceinline__ float sumsq8(uint4 v, float acc) {
-  const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
   float se = acc, so = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "fma.rn.f32.bf16 %0, lo, lo, %0;\n\tfma.rn.f32.bf16 %1, hi, hi, %1;\n\t}"
-        : "+f"(se), "+f"(so)
-        : "r"(w4[i]));
+  sq_acc_bf2(v.x, se, so);
+  sq_acc_bf2(v.y, se, so);
+  sq_acc_bf2(v.z, se, so);
+  sq_acc_bf2(v.w, se, so);
   return se + so;
 }
 

@@ -636,15 +636,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int srow = q * 32 + lane;  // the lane's row in the side tile
       if (hn) {
         // q_norm / k_norm: Qwen3RMSNorm over the row's 128 values of this head
-        float2 s2 = make_float2(0.0f, 0.0f);
+        float se = 0.0f, so = 0.0f;  // even / odd columns' sums of squares
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float2 f = bf2_f2(y[c][k]);
-            s2 = fma_f2(f, f, s2);
-          }
-        const float rinv = __frsqrt_rn(__fadd_rn(__fdiv_rn(__fadd_rn(s2.x, s2.y), 128.0f), p.hn_eps));
+          for (int k = 0; k < 16; ++k) sq_acc_bf2(y[c][k], se, so);
+        // mean = sum / 128 as an exact power-of-two scaling (the same rounding as the division)
+        const float rinv = __frsqrt_rn(__fadd_rn(__fmul_rn(__fadd_rn(se, so), 0.0078125f), p.hn_eps));
         const float2 r2 = make_float2(rinv, rinv);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
