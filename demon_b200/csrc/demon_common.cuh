@@ -217,6 +217,11 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t a) {
                : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_shared_s32(uint32_t a) {
+  int v;
+  asm volatile("ld.shared.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_shared_f32(uint32_t a, float x) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(x) : "memory");
 }

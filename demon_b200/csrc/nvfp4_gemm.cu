@@ -117,7 +117,8 @@ struct GemmCfg {
   // (at most two) gate rows its 128 rows use
   static constexpr int kSideRow = 272;
   static constexpr int kSideGate = 4 * kBM * 128;  // offset of the gate segments (SIDE 2)
-  static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 : 0;
+  // (SIDE 2: then one int, the first row of the tile's second gate row)
+  static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 + 16 : 0;
   static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
   static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
   static constexpr int offHn = offCol + (kColVec ? kEpiWarps * (BN / 2) * 4 : 0);  // head-norm weight per warp
@@ -480,6 +481,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // gate rows of this CTA's rows inside M (gate_rows >= 128: one or two)
         const int g0 = m0 / (int)p.gate_rows;
         const int ng = (p.gate && m0 < p.M) ? (min(m0 + kBM, p.M) - 1) / (int)p.gate_rows - g0 + 1 : 0;
+        // the epilogue's split between the two gate rows, published by the arrive below
+        *reinterpret_cast<int*>(side + C::kSideGate + 2 * BN * 2) = (g0 + 1) * (int)p.gate_rows;
         mbar_arrive_expect_tx(side_full, 4u * kBM * 128u + (uint32_t)ng * (BN * 2));
         for (int b = 0; b < 4; ++b) tma_load_2d(side + b * (kBM * 128), &tmR, side_full, n0 + 64 * b, m0);
         for (int i = 0; i < ng; ++i)
@@ -694,9 +697,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the side tile and stored from there, one 32-row x 64-column TMA box (the 128-byte
         // swizzle it was loaded with) per two chunks; the gate from its segments in the tile
         const bool gated = p.gate != nullptr;
-        // the lane's gate row: the tile's first or second (a gate row spans >= 128 rows)
-        const int gr = gated ? (int)p.gate_rows : 1;
-        const int gnext = (m0 / gr + 1) * gr;  // first row of the second gate row (warp-uniform)
+        // the lane's gate row: the tile's first or second (a gate row spans >= 128 rows); the
+        // loader stored the first row of the second one with the tile
+        const int gnext = gated ? ld_shared_s32(side + C::kSideGate + 2 * BN * 2) : 0;
         const int gsel = (gated && (int)min(row, (int64_t)p.M - 1) >= gnext) ? 1 : 0;
         const uint32_t gb = side + C::kSideGate + gsel * (BN * 2) + half * (C::kColsPerWarp * 2);
 #pragma unroll
