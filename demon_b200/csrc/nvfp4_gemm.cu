@@ -93,7 +93,7 @@ static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads *
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
 // SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual, 3 none and
-// no per-column vector either (no bias, no head norm: the space goes to a fifth stage)
+// no per-column vector either (no bias: the space goes to a fifth stage)
 template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 struct GemmCfg {
   static constexpr bool kSideTile = SIDE == 1 || SIDE == 2;
@@ -121,8 +121,9 @@ struct GemmCfg {
   static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 + 16 : 0;
   static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
   static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
-  static constexpr int offHn = offCol + (kColVec ? kEpiWarps * (BN / 2) * 4 : 0);  // head-norm weight per warp
-  static constexpr int offBar = offHn + (FP4 && SIDE != 2 && SIDE != 3 ? kEpiWarps * (BN / 2) * 4 : 0);
+  static constexpr int offHn = offCol + (kColVec ? kEpiWarps * (BN / 2) * 4 : 0);
+  // head-norm weight per warp: its 128 columns as 64 bf16 pairs
+  static constexpr int offBar = offHn + (FP4 && SIDE != 2 ? kEpiWarps * (BN / 2) * 2 : 0);
   static constexpr int kBars = 2 * STAGES + 3 + (kSideTile ? 2 : 0);
   static constexpr int offMisc = offBar + kBars * 8;
   static constexpr int kSmem = offMisc + 16 + 1024;  // + alignment slack
@@ -506,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // which half of the tile's columns
     const uint32_t stg = smem_u32(smem + C::offStg + ew * C::kStgWarp);
     const uint32_t colv = smem_u32(smem + C::offCol) + ew * (C::kColsPerWarp * 4);
-    const uint32_t hnv = smem_u32(smem + C::offHn) + ew * (C::kColsPerWarp * 4);
+    const uint32_t hnv = smem_u32(smem + C::offHn) + ew * (C::kColsPerWarp * 2);
     if (FP4 && lane == 0) prefetch_tmap(&tmO);
     const uint64_t out_policy = l2_policy_evict_first();
     uint32_t it = 0, nstore = 0;
@@ -1101,9 +1102,9 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
                           (uint64_t)a->ldo * 2, 64, 32));
     return launch_gemm<256, 4, true, true, 2>(ta, tb, tla, tlb, to2, p, st, &tsfa, &tsfb, &tr);
   }
-  // no bias, head norm or residual: no per-column vector, and its shared memory buys a fifth
+  // no bias (and no side tile above): no per-column vector, and its shared memory buys a fifth
   // stage (the SwiGLU gate/up GEMM: 1190 -> 985 us at M = 96,000)
-  if (pair && !a->bias && a->hn_cols == 0)
+  if (pair && !a->bias)
     return launch_gemm<256, 5, true, true, 3>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
