@@ -237,3 +237,27 @@ def test_side_tile_matches_direct_path(cuda, tmp_path):
     for k in outs["1"]:
         assert torch.isfinite(outs["1"][k]).all(), k
         assert torch.equal(outs["1"][k], outs["0"][k]), k
+
+
+@pytest.mark.parametrize("gate_rows", [None, 7, 750])
+def test_inplace_residual_matches_separate_output(cuda, gate_rows):
+    """out == residual (a residual stream updated in place, which the C ABI allows): each tile's
+    residual is read before its output is stored, so the bits equal those of a separate output,
+    with no gate, a per-7-rows gate (direct reads) or a per-sequence gate (the residual side
+    tile), at an M that leaves the last CTA pair partly empty."""
+    from demon_b200 import nvfp4
+    M, N, K = 3001, 2048, 2048
+    g = torch.Generator(device=cuda).manual_seed(41)
+    x = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    w = nvfp4.pack_weight(weight(N, K, seed=42, std=0.05, dev=cuda))
+    res = torch.randn(M, N, generator=g, device=cuda).to(torch.bfloat16)
+    kw = {}
+    if gate_rows is not None:
+        kw = dict(gate=torch.randn((M + gate_rows - 1) // gate_rows, N, generator=g, device=cuda).to(torch.bfloat16),
+                  gate_rows=gate_rows)
+    a = nvfp4.quantize(x)
+    ref = nvfp4.gemm(a, w, residual=res, **kw)
+    h = res.clone()
+    y = nvfp4.gemm(a, w, residual=h, out=h, **kw)
+    assert y.data_ptr() == h.data_ptr()
+    assert torch.equal(h, ref)
