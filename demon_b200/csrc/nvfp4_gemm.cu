@@ -93,11 +93,12 @@ static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads *
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
 // SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual, 3 none and
-// no per-column vector either (no bias: the space goes to a fifth stage)
+// no per-column vector either (no bias: the space goes to a fifth stage), 5 as 3 with the bias
+// read from global memory in the epilogue (a separate kernel: 3's code stays as it is)
 template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 struct GemmCfg {
   static constexpr bool kSideTile = SIDE == 1 || SIDE == 2;
-  static constexpr bool kColVec = SIDE != 3;  // bias / column scale staged per warp
+  static constexpr bool kColVec = SIDE != 3 && SIDE != 5;  // bias / column scale staged per warp
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
   static constexpr int kSFA = FP4 ? 2048 : 0;
@@ -591,7 +592,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < C::kChunks; ++c) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 cv = C::kColVec ? ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          float4 cv = make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (C::kColVec) {
+            cv = ld_shared_f32x4(colv + 4 * (c * 32 + 4 * j));
+          } else if constexpr (SIDE == 5) {  // four bias values, the same for every lane
+            const int i0 = c * 32 + 4 * j;
+            const int n = sm ? n0 + (i0 < 64 ? half * 64 + i0 : 128 + half * 64 + (i0 - 64)) : ncol0 + i0;
+            const uint2 b2 = __ldg(reinterpret_cast<const uint2*>(p.bias + n));
+            cv = make_float4(bf16_lo(b2.x), bf16_hi(b2.x), bf16_lo(b2.y), bf16_hi(b2.y));
+          }
           if (FP4) {
             const float ac = (sm && c >= 2) ? alpha_u : alpha;
             const float2 al = make_float2(ac, ac);
@@ -1106,6 +1115,8 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   // stage (the SwiGLU gate/up GEMM: 1190 -> 985 us at M = 96,000)
   if (pair && !a->bias)
     return launch_gemm<256, 5, true, true, 3>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
+  if (pair && !a->residual)  // a bias but no residual (config 1's linear): the bias from global memory
+    return launch_gemm<256, 5, true, true, 5>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (pair) return launch_gemm<256, 4, true, true>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (bn256) return launch_gemm<256, 3, true>(ta, tb, tla, tlb, to, p, st);
   return launch_gemm<128, 5, true>(ta, tb, tla, tlb, to, p, st);
