@@ -490,7 +490,7 @@ def linear_leg(dev, stream, reps=64):
     f = ROOT / "profiles" / "traffic.json"
     if f.exists():
         traffic = json.loads(f.read_text()).get("nvfp4_gemm_config1")
-    return {"kernel": "demon::gemm_kernel<256, 4, 1, 1, 0>", "workload": CONFIG1["workload"], "us": us,
+    return {"kernel": "demon::gemm_kernel<256, 5, 1, 1, 5>", "workload": CONFIG1["workload"], "us": us,
             "achieved": tf, "unit": "TFLOP/s", "peak": pk["fp4_tflops"], "frac": tf / pk["fp4_tflops"],
             "peak_note": "4x the measured burst bf16 cuBLAS figure (kernel timed alone)", "traffic": traffic}
 
@@ -619,7 +619,7 @@ def run_linear(args):
                          "peak_note": f"FP4 dense peak taken as 4x the {pk['source']} bf16 cuBLAS figure "
                                       f"({pk['bf16_tflops']:.0f} TF/s); nominal 9 PF/s -> frac "
                                       f"{achieved / 9000.0:.3f}",
-                         "kernel": "demon::gemm_kernel<256, 4, 1, 1, 0>", "gemm_us": gemm_avg * 1e3},
+                         "kernel": "demon::gemm_kernel<256, 5, 1, 1, 5>", "gemm_us": gemm_avg * 1e3},
             "e2e": {"value": FLOP1 * args.steps * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": M1 * K1 * 2, "d2h_bytes_per_step": M1 * N1 * 2},
             "gpu_launches": 2 * args.steps + gemm_reps * nsets,
