@@ -188,6 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::offMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // programmatic dependent launch: the next kernel in the stream may be scheduled now (it can only
+  // use SMs this grid leaves, and it waits for this grid to complete before touching memory)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int KT = p.K / C::kStepElems;
   const int lboxes = p.lora_rank > 0 ? (p.lora_rank + 63) / 64 : 0;
   const int num_tiles = p.m_tiles * p.n_tiles;
@@ -260,6 +263,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // the set-up above (barriers, tensor memory, tensor-map prefetch) overlaps the previous kernel's
+  // tail; every global read and write comes after that kernel has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (warp < 4) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kGemmIssueRegs));
    if (warp == 0) {
@@ -914,13 +920,15 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& l
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // griddepcontrol in the kernel
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   DEMON_CUDA(cudaLaunchKernelEx(&cfg, kern, a, b, la, lb, o, sfa ? *sfa : z, sfb ? *sfb : z, res ? *res : z, p));
   return DEMON_OK;
 }
