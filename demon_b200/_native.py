@@ -60,7 +60,7 @@ class DemonGemmArgs(ctypes.Structure):
         ("gate", _vp), ("gate_rows", _i64), ("ld_gate", _i64),
         ("lora_xa", _vp), ("lora_b", _vp), ("lora_rank", _i64),
         ("hn_cols", _i64), ("hn_q_cols", _i64), ("rope_S", _i64), ("hn_wq", _vp), ("hn_wk", _vp),
-        ("rope_cos", _vp), ("rope_sin", _vp), ("hn_eps", _f32), ("silu_mul", _i32),
+        ("rope_cos", _vp), ("rope_sin", _vp), ("hn_eps", _f32), ("silu_mul", _i32), ("rope_half", _i32),
     ]
 
 

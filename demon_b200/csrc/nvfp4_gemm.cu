@@ -112,14 +112,14 @@ struct GemmCfg {
   static constexpr int kStgWarp = SIDE == 2 ? 0 : FP4 ? 4096 : 32 * kStgPitch;
   static constexpr int offStg = (offSFB + STAGES * kSFB + 1023) / 1024 * 1024;
   // side-input tile (SIDE kernels), loaded by a loader warp and read row by row: the rotary
-  // tables of the CTA's 128 rows (cos rows, then sin rows: 256 bytes at a 272-byte pitch, so
-  // that a warp's row-per-lane 16-byte reads are conflict-free), or the residual tile (four
-  // 128-row x 64-column TMA boxes with the 128-byte swizzle) and the tile's segments of the
-  // (at most two) gate rows its 128 rows use
+  // tables of the CTA's 128 rows (tables with equal halves: per row the 64-column cos half and
+  // the sin half, 256 bytes at a 272-byte pitch, so that a warp's row-per-lane 16-byte reads
+  // are conflict-free), or the residual tile (four 128-row x 64-column TMA boxes with the
+  // 128-byte swizzle) and the tile's segments of the (at most two) gate rows its 128 rows use
   static constexpr int kSideRow = 272;
   static constexpr int kSideGate = 4 * kBM * 128;  // offset of the gate segments (SIDE 2)
   // (SIDE 2: then one int, the first row of the tile's second gate row)
-  static constexpr int kSide = SIDE == 1 ? 2 * kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 + 16 : 0;
+  static constexpr int kSide = SIDE == 1 ? kBM * kSideRow : SIDE == 2 ? kSideGate + 2 * BN * 2 + 16 : 0;
   static constexpr int offSide = offStg + kEpiWarps * kStgWarp;  // 1024-aligned (SW128 boxes)
   static constexpr int offCol = offSide + kSide;                 // fp32 per-column vector per warp
   static constexpr int offHn = offCol + (kColVec ? kEpiWarps * (BN / 2) * 4 : 0);
@@ -454,9 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ side-input loader
     // At the first tile of each run of tiles with one side key, once the epilogue warps have
     // released the previous side tile: the table rows of the m-block by coalesced 16-byte
-    // cp.async copies, half a warp per 256-byte row (positions wrap at rope_S inside a tile;
-    // rows past M are skipped), or the residual tile by four TMA boxes (rows past M read as
-    // zeros).
+    // cp.async copies, half a warp per row (the cos and sin halves; positions wrap at rope_S
+    // inside a tile; rows past M are skipped), or the residual tile by four TMA boxes (rows
+    // past M read as zeros).
     constexpr bool side_rope = SIDE == 1;
     uint8_t* side = smem + C::offSide;
     uint32_t sit = 0;  // side tiles issued
@@ -473,12 +473,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(side_empty, (sit & 1u) ^ 1u, abort_flag, t0, p.status, 10, lim)) break;
       if (side_rope) {
         const int rows = max(0, min(kBM, p.M - m0));
-        const int hl = lane >> 4, ch = lane & 15;  // row parity, 16-byte chunk of the row
+        const int hl = lane >> 4, ch = lane & 15;  // row parity, 16-byte chunk of the staged row
         const uint32_t sb = smem_u32(side);
+        const __nv_bfloat16* tab = (ch < 8 ? p.rope_cos : p.rope_sin) + (ch & 7) * 8;
         int64_t pos = ((int64_t)m0 + hl) % p.rope_S;
         for (int r = hl; r < rows; r += 2) {
-          cp_async_16(sb + r * C::kSideRow + ch * 16, p.rope_cos + pos * 128 + ch * 8);
-          cp_async_16(sb + (kBM + r) * C::kSideRow + ch * 16, p.rope_sin + pos * 128 + ch * 8);
+          cp_async_16(sb + r * C::kSideRow + ch * 16, tab + pos * 128);
           pos += 2;
           while (pos >= p.rope_S) pos -= p.rope_S;
         }
@@ -678,17 +678,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t pos = row % p.rope_S;
           const uint4* cr = reinterpret_cast<const uint4*>(p.rope_cos + pos * 128);
           const uint4* sr = reinterpret_cast<const uint4*>(p.rope_sin + pos * 128);
-          const uint32_t cb = side + srow * C::kSideRow, sb = side + (kBM + srow) * C::kSideRow;
+          const uint32_t cb = side + srow * C::kSideRow, sb = cb + 128;  // staged cos / sin halves
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               uint4 c1, c2, s1, s2v;
-              if (side_rope) {
-                c1 = ld_shared_v4(cb + (c * 4 + j) * 16);
-                c2 = ld_shared_v4(cb + (8 + c * 4 + j) * 16);
-                s1 = ld_shared_v4(sb + (c * 4 + j) * 16);
-                s2v = ld_shared_v4(sb + (8 + c * 4 + j) * 16);
+              if (side_rope) {  // equal halves: columns i and i + 64 share their values
+                c1 = c2 = ld_shared_v4(cb + (c * 4 + j) * 16);
+                s1 = s2v = ld_shared_v4(sb + (c * 4 + j) * 16);
               } else {
                 c1 = __ldg(cr + c * 4 + j);
                 c2 = __ldg(cr + 8 + c * 4 + j);
@@ -1104,13 +1102,14 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // A side tile when the epilogue would otherwise read per-row operands one row per lane
   // (gemm_check: never both, never with SwiGLU; residual rows 16-byte aligned): the rotary
-  // tables of the head-norm + RoPE epilogue (68 KB: three stages), or the residual, which the
-  // output overwrites and is stored from (no staging buffers: four stages, 64 x 32 store
-  // boxes), with the gate rows when each spans at least a tile's 128 rows
-  const bool side_rope = a->rope_cos && a->hn_cols > 0;
+  // tables of the head-norm + RoPE epilogue when their halves are equal (rope_half: 34 KB, four
+  // stages; full tables are read directly), or the residual, which the output overwrites and
+  // is stored from (no staging buffers: four stages, 64 x 32 store boxes), with the gate rows
+  // when each spans at least a tile's 128 rows
+  const bool side_rope = a->rope_cos && a->hn_cols > 0 && a->rope_half;
   const bool side_res = a->residual != nullptr && (!a->gate || a->gate_rows >= 128);
   if (pair && side_stage_enabled() && side_rope)
-    return launch_gemm<256, 3, true, true, 1>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
+    return launch_gemm<256, 4, true, true, 1>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (pair && side_stage_enabled() && side_res) {
     CUtensorMap tr, to2;
     DEMON_RC(make_tmap_2d(&tr, a->residual, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)N, (uint64_t)M,

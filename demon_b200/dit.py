@@ -219,7 +219,8 @@ class Attention(nn.Module):
     def self_attn(self, a, xb, h, gate, B, S, rope):
         hd, hq, hk = self.head_dim, self.hq, self.hk
         cos, sin = rope
-        qkv = self._proj([self.q_proj, self.k_proj, self.v_proj], a, xb, rope=(cos, sin, S))  # [M, (hq+2hk)*hd]
+        # the tables are cat(freqs, freqs).cos() / .sin() (DemonDiT._rope): equal halves
+        qkv = self._proj([self.q_proj, self.k_proj, self.v_proj], a, xb, rope=(cos, sin, S, True))  # [M, (hq+2hk)*hd]
         ld = qkv.stride(0)
         q = qkv.as_strided((B, S, hq, hd), (S * ld, ld, hd, 1))
         k = qkv.as_strided((B, S, hk, hd), (S * ld, ld, hd, 1), hq * hd)

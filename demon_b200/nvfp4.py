@@ -168,7 +168,9 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
 
     ``head_norm = (hn_cols, hn_q_cols, w_q, w_k, eps)``: per-head RMSNorm of the output's
     first hn_cols columns (heads of 128; w_q for the first hn_q_cols, w_k after), and with
-    ``rope = (cos, sin, S)`` the rotary embedding after it (q/k projections of the DiT).
+    ``rope = (cos, sin, S[, half])`` the rotary embedding after it (q/k projections of the DiT);
+    ``half`` promises that the tables' two 64-column halves are equal (the standard
+    rotate-half embedding), so that only the first half is read.
     """
     if a.K != w.K:
         raise ValueError(f"K mismatch: activations {a.K} vs weight {w.K}")
@@ -199,8 +201,9 @@ def gemm(a: NVFP4Tensor, w: NVFP4Tensor, bias: torch.Tensor | None = None,
         args.hn_cols, args.hn_q_cols, args.hn_wq, args.hn_wk = hn_cols, hn_q, nat.ptr(wq), nat.ptr(wk)
         args.hn_eps = float(eps)
         if rope is not None:
-            cos, sin, S = rope
+            cos, sin, S = rope[:3]
             args.rope_cos, args.rope_sin, args.rope_S = nat.ptr(cos), nat.ptr(sin), int(S)
+            args.rope_half = int(len(rope) > 3 and bool(rope[3]))
     nat.check(nat.load().demon_nvfp4_gemm(ctypes.byref(args), nat.stream_ptr(stream)))
     return out
 

@@ -144,6 +144,10 @@ typedef struct DemonGemmArgs {
    * demon_silu_mul_quantize's h.  Needs N % 256 == 0; excludes LoRA, head norm, gate,
    * residual. */
   int32_t silu_mul;
+  /* rope_half != 0: the caller guarantees that columns 64..127 of rope_cos / rope_sin equal
+   * columns 0..63 (the standard rotate-half embedding, cat(freqs, freqs)); only the first 64
+   * columns are read, and the epilogue stages half the table (a faster kernel form). */
+  int32_t rope_half;
 } DemonGemmArgs;
 
 DEMON_API int demon_nvfp4_gemm(const DemonGemmArgs* args, void* stream);

@@ -140,7 +140,7 @@ def test_head_norm_rope_epilogue_at_tick_size(cuda):
     emb = torch.cat([pos[:, None] * inv[None]] * 2, -1)
     cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
     hn = ((hq + hk) * 128, hq * 128, wq.to(cuda), wk.to(cuda), eps)
-    rp = (cos.to(cuda), sin.to(cuda), S_TOK)
+    rp = (cos.to(cuda), sin.to(cuda), S_TOK, True)  # cat(freqs, freqs): equal halves (the side tile)
     y = nvfp4.gemm(nvfp4.quantize(x), fused, head_norm=hn, rope=rp)
     seqs = [0, 50, M // S_TOK - 1]
     rows = torch.cat([torch.arange(s * S_TOK, (s + 1) * S_TOK) for s in seqs])
@@ -211,6 +211,9 @@ out = {
     "res_gate150": Q.gemm(a, w1, residual=res, gate=gate150, gate_rows=150),
     "res_plain": Q.gemm(a, w1, residual=res),
     "rope": Q.gemm(a, wqkv, head_norm=((hq + hk) * 128, hq * 128, wq, wk, 1e-6), rope=(cos, sin, S)),
+    "rope_half": Q.gemm(a, wqkv, head_norm=((hq + hk) * 128, hq * 128, wq, wk, 1e-6),
+                        rope=(torch.cat([cos[:, :64]] * 2, -1).contiguous(), torch.cat([sin[:, :64]] * 2, -1).contiguous(),
+                              S, True)),
 }
 torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[2])
 """
@@ -261,3 +264,25 @@ def test_inplace_residual_matches_separate_output(cuda, gate_rows):
     y = nvfp4.gemm(a, w, residual=h, out=h, **kw)
     assert y.data_ptr() == h.data_ptr()
     assert torch.equal(h, ref)
+
+
+def test_rope_half_tables_match_full_tables(cuda):
+    """rope_half (tables whose 64-column halves are equal; only the first half is read and the
+    side tile stages half rows) gives the bits of the full tables read directly, at an M whose
+    tiles straddle sequence boundaries and leave the last CTA pair partly empty."""
+    from demon_b200 import nvfp4
+    M, K, S, hq, hk = 3001, 1024, 750, 4, 2
+    g = torch.Generator(device=cuda).manual_seed(51)
+    x = torch.randn(M, K, generator=g, device=cuda).to(torch.bfloat16)
+    w = nvfp4.pack_weight(weight((hq + 2 * hk) * 128, K, seed=52, std=0.05, dev=cuda))
+    wq = (1 + 0.1 * torch.randn(128, generator=g, device=cuda)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(128, generator=g, device=cuda)).to(torch.bfloat16)
+    half_c = torch.randn(S, 64, generator=g, device=cuda).to(torch.bfloat16)
+    half_s = torch.randn(S, 64, generator=g, device=cuda).to(torch.bfloat16)
+    cos, sin = torch.cat([half_c, half_c], -1).contiguous(), torch.cat([half_s, half_s], -1).contiguous()
+    a = nvfp4.quantize(x)
+    hn = ((hq + hk) * 128, hq * 128, wq, wk, 1e-6)
+    full = nvfp4.gemm(a, w, head_norm=hn, rope=(cos, sin, S))
+    half = nvfp4.gemm(a, w, head_norm=hn, rope=(cos, sin, S, True))
+    assert torch.isfinite(full).all()
+    assert torch.equal(half, full)
