@@ -92,13 +92,13 @@ static_assert(128 * kGemmIssueRegs + 32 * kEpiWarps * kGemmEpiRegs <= kThreads *
               "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
 constexpr int kStgPitch = 80;     // bf16-GEMM transpose staging: 32 bf16 + 16 bytes of padding per row
 
-// SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual, 3 none and
-// no per-column vector either (no bias: the space goes to a fifth stage), 5 as 3 with the bias
-// read from global memory in the epilogue (a separate kernel: 3's code stays as it is)
+// SIDE: 0 no side tile, 1 the rotary tables (head norm + RoPE), 2 the residual (no bias), 3
+// none and no per-column vector either (no bias: the space goes to a fifth stage), 5 as 3 with
+// the bias read from global memory in the epilogue (a separate kernel: 3's code stays as it is)
 template <int BN, int STAGES, bool FP4, bool PAIR = false, int SIDE = 0>
 struct GemmCfg {
   static constexpr bool kSideTile = SIDE == 1 || SIDE == 2;
-  static constexpr bool kColVec = SIDE != 3 && SIDE != 5;  // bias / column scale staged per warp
+  static constexpr bool kColVec = SIDE == 0 || SIDE == 1;  // bias / column scale staged per warp
   static constexpr int kA = kBM * kRowBytes;
   static constexpr int kB = (PAIR ? BN / 2 : BN) * kRowBytes;  // a CTA pair splits the B tile
   static constexpr int kSFA = FP4 ? 2048 : 0;
@@ -1107,7 +1107,7 @@ extern "C" int demon_nvfp4_gemm(const DemonGemmArgs* a, void* stream) {
   // is stored from (no staging buffers: four stages, 64 x 32 store boxes), with the gate rows
   // when each spans at least a tile's 128 rows
   const bool side_rope = a->rope_cos && a->hn_cols > 0 && a->rope_half;
-  const bool side_res = a->residual != nullptr && (!a->gate || a->gate_rows >= 128);
+  const bool side_res = a->residual != nullptr && !a->bias && (!a->gate || a->gate_rows >= 128);
   if (pair && side_stage_enabled() && side_rope)
     return launch_gemm<256, 4, true, true, 1>(ta, tb, tla, tlb, to, p, st, &tsfa, &tsfb);
   if (pair && side_stage_enabled() && side_res) {
