@@ -167,3 +167,26 @@ def test_stream_equals_batch_banded_gemm_order(cuda):
         assert torch.isfinite(alone.float()).all(), i
         assert torch.equal(outs[i], alone), f"request {i}: banded stream and batch paths differ"
     assert not torch.equal(outs[0], outs[1])
+
+
+def test_batched_modulation_equals_per_layer(cuda):
+    """The model computes every layer's AdaLN modulation (table + temb, 1 + scale, the shifts)
+    in batched ops and hands each layer its slices; a layer that computes its own modulation
+    gives the same bits."""
+    dec = _decoder(cuda)
+    g = torch.Generator(device=cuda).manual_seed(7)
+    B, S, H = 2, 15, SMALL["hidden_size"]
+    h = torch.randn(B * S, H, generator=g, device=cuda).to(torch.bfloat16)
+    tproj = (0.1 * torch.randn(B, 6, H, generator=g, device=cuda)).to(torch.bfloat16)
+    enc = torch.randn(B, L, H, generator=g, device=cuda).to(torch.bfloat16)
+    kv, Lk = dec.encoder_kv(enc)
+    rope = dec._rope(S, cuda, torch.bfloat16)
+    mods = torch.stack([l.scale_shift_table[0] for l in dec.layers]).unsqueeze(1) + tproj.unsqueeze(0)
+    scales1 = mods[:, :, 1::3] + 1
+    shifts = mods[:, :, 0::3].contiguous()
+    with torch.no_grad():
+        for i, (layer, kv_l) in enumerate(zip(dec.layers, kv)):
+            ada = (mods[i, :, 2], mods[i, :, 5], scales1[i, :, 0], scales1[i, :, 1], shifts[i, :, 0], shifts[i, :, 1])
+            a = layer(h.clone(), tproj, kv_l, B, S, Lk, rope, ada)
+            b = layer(h.clone(), tproj, kv_l, B, S, Lk, rope)
+            assert torch.equal(a, b), i
