@@ -1422,7 +1422,7 @@ def run_kernel_workload(args):
         pos = torch.arange(S, dtype=torch.float32, device=dev)
         inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev).float() / 128))
         emb = torch.cat([pos[:, None] * inv[None]] * 2, -1)
-        rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16), S)
+        rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16), S, True)  # equal halves, as the DiT's
         o4, o2 = (torch.empty(M, n, dtype=torch.bfloat16, device=dev) for n in (4096, 2048))
         o6 = torch.empty(M, 6144, dtype=torch.bfloat16, device=dev)
         o12 = torch.empty(M, 12288, dtype=torch.bfloat16, device=dev)
