@@ -1,28 +1,33 @@
 // nvfp4_gemm.cu -- tcgen05 block-scaled NVFP4 GEMM with fused epilogue (sm_100a),
 // and the bf16 tcgen05 GEMM used for the LoRA down-projection.
 //
-// Persistent kernel: one CTA per SM walks output tiles of 128 x BN
-// (tile t = blockIdx.x + i * gridDim.x, M fastest so concurrent CTAs share the
-// B tiles in L2).  Warp roles (320 threads):
-//   warp 0      TMA producer: A/B tiles with tiled TMA loads (128-byte swizzle,
-//               no multicast) and the stage's block scales with untiled bulk
-//               copies -- the quantiser writes scales in the tcgen05 128x4-chunk
-//               layout, so a stage's scales are contiguous.  It runs ahead into
-//               the next tile while the epilogue drains the current one.
-//   warp 1      TMEM allocation + one MMA-issuing thread: per stage it copies
-//               the scales SMEM -> TMEM (tcgen05.cp 32x128b.warpx4, replicated
-//               into the four lane quadrants), issues four
-//               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
-//               and commits to the stage's "empty" barrier.
-//   warps 2-9   epilogue, two warps per TMEM lane quadrant, each owning half of
-//               the tile's columns.  Bias, row scales and L2 prefetches of the
-//               gate / residual rows are issued while the MMAs run; then the
-//               warps drain their accumulator columns into registers with
-//               tcgen05.ld and release TMEM at once (the MMA warp starts the
-//               next tile), convert each row to bf16 (alpha * acc + bias, one
-//               rounding), apply gate and residual in bf16 as the reference's
-//               eager ops do, and write 32x32 blocks through a double-buffered,
-//               64-byte-swizzled staging area with asynchronous TMA stores.
+// Persistent kernel: one CTA per SM (for N % 256 == 0 a 2-CTA cluster per SM pair, cta_group::2
+// MMAs on 256 x 256 tiles) walks output tiles in bands of m-blocks swept over N (or, for the
+// rotary side tile, contiguous tiles with N fastest).  Warp roles (384 threads, three
+// warpgroups; setmaxnreg gives the first 56 registers per thread and the other two 224):
+//   warp 0      TMA producer: A/B tiles with tiled TMA loads (128-byte swizzle, no
+//               multicast) and the stage's block scales -- the quantiser writes scales in
+//               the tcgen05 128x4-chunk layout, so a stage's scales are contiguous.  It runs
+//               ahead into the next tile while the epilogue drains the current one.
+//   warp 1      TMEM allocation + one MMA-issuing thread: per stage it copies the scales
+//               SMEM -> TMEM (tcgen05.cp 32x128b.warpx4, replicated into the four lane
+//               quadrants), issues four tcgen05.mma.kind::mxf4nvf4.block_scale.block16
+//               (K = 64 each) and commits to the stage's "empty" barrier.
+//   warp 2      side-input loader (SIDE 1 / 2): the rotary table rows or the residual tile
+//               (with the tile's gate rows) into shared memory, so that the epilogue reads
+//               its per-row operands from there and not one row per lane from global memory.
+//   warp 3      idle.
+//   warps 4-11  epilogue, two warps per TMEM lane quadrant, each owning half of the tile's
+//               columns.  Per-column vectors and row scales are fetched while the MMAs run;
+//               the warps drain their accumulator columns with tcgen05.ld and release TMEM at
+//               once (the MMA warp starts the next tile), convert each row to bf16 (alpha *
+//               acc + bias, one rounding), apply head norm + RoPE, SwiGLU, gate and residual in
+//               bf16 as the reference's eager ops do, and write 32x32 blocks through a
+//               double-buffered, 64-byte-swizzled staging area with TMA stores (the residual
+//               mode writes over the staged residual and stores 32x64 boxes from there).
+// Modes (the SIDE template argument, chosen per call on the host): 0 plain (4 stages), 1 the
+// rotary side tile, 2 the residual side tile, 3 no per-column vector (no bias: 5 stages), 5 as
+// 3 with the bias read from global memory.  Pair launches allow programmatic dependent launch.
 // Hot LoRA: for each 64-wide slice of the rank, one extra pipeline stage holds
 // the xa tile (128 x 64 bf16, 16 KB -- the size of an A stage) and the
 // lora_b tile (BN x 64 bf16 -- the size of a B stage); four kind::f16 MMAs
