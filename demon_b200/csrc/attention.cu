@@ -67,9 +67,11 @@ constexpr int kWarpStg = 2 * 32 * 128;       // one epilogue warp's 32-row O sta
 constexpr int kThreads = 512;           // four warpgroups
 
 // Registers per thread after the split (setmaxnreg): the launch gives 512 x 128; the two
-// softmax warpgroups take 176, the epilogue warpgroup 96, the TMA / MMA warpgroup 64:
-// 256 * 176 + 128 * 96 + 128 * 64 = 65,536 = 512 * 128.
-constexpr int kLaunchRegs = 128, kSoftmaxRegs = 176, kEpilogueRegs = 96, kIssueRegs = 64;
+// softmax warpgroups take 176, the epilogue warpgroup 56, the TMA / MMA warpgroup 104:
+// 256 * 176 + 128 * 56 + 128 * 104 = 63,536 <= 512 * 128.  No role spills at these counts;
+// the issue warpgroup (descriptors and ring phases of both loops) is the one that spilled at
+// 64 (176 bytes), which delayed MMA issue: band attention 394 -> 383 us, global 563 -> 556 us.
+constexpr int kLaunchRegs = 128, kSoftmaxRegs = 176, kEpilogueRegs = 56, kIssueRegs = 104;
 static_assert(256 * kSoftmaxRegs + 128 * kEpilogueRegs + 128 * kIssueRegs <= kThreads * kLaunchRegs,
               "register split exceeds the launch's registers (setmaxnreg.inc would wait for good)");
 
