@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
   const bool cta_live = m_first < a.M;
   const int64_t b0 = cta_live ? m_first / a.rows_per_mod : 0;
   const int64_t b1 = cta_live ? min(m_first + G::R * RPW - 1, a.M - 1) / a.rows_per_mod : 0;
+  const int64_t m_b1 = (b0 + 1) * a.rows_per_mod;  // first row of modulation row b0 + 1
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
   uint4 xv[2 * G::NB];
   auto load_row = [&](int64_t m) {
@@ -229,7 +230,9 @@ __global__ void __launch_bounds__(256, 3) adanorm_warp_kernel(const NormArgs a) 
     for (int j = 0; j < 2 * G::NB; ++j) ss = sumsq8(xv[j], ss);
     ss = warp_sum(ss);
     const float rinv = __frsqrt_rn(__fadd_rn(mean_of_sum<D>(ss), a.eps));
-    const int sel = (!pad && (MUL || ADD) && m / a.rows_per_mod != b0) ? 1 : 0;
+    // m >= m_first >= b0 * rows_per_mod, so m / rows_per_mod != b0 is m >= m_b1 (a compare, not
+    // a 64-bit division per row)
+    const int sel = (!pad && (MUL || ADD) && m >= m_b1) ? 1 : 0;
     uint32_t mb[2 * G::NB];
 #pragma unroll
     for (int j = 0; j < G::NB; ++j) {
