@@ -90,11 +90,31 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 64, kColO = 256;  // S_h at 128 h, P_h at 128 h + 64, O_h at 256 + 128 h
 constexpr float kRescaleLog2 = 8.0f;                    // lazy rescale threshold (log2 units)
 
+// Division by a divisor fixed for the launch (Granlund and Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994, theorem 4.2): with l = ceil(log2 d), s = 31 + l and
+// m = ceil(2^s / d), floor(n / d) = (n * m) >> s for every 0 <= n < 2^31 (m * d - 2^s < d <=
+// 2^(s - 31)), and m < 2^32.  The work-unit decode below runs at every unit boundary in each
+// role, the MMA thread's between one unit's last P V and the next unit's first Q K^T; a 64-bit
+// division there is a long dependent instruction sequence.
+struct FastDiv {
+  uint32_t d, m, s;
+};
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 32 && (1ull << l) < d) ++l;
+  const uint32_t s = 31 + l;
+  return FastDiv{d, (uint32_t)(((1ull << s) + d - 1) / d), s};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)n * f.m) >> f.s);
+}
+
 struct Params {
   int B, S, L, Hk, G, window;  // window < 0: no band
   int n_qblk, n_kblk, pairs;   // blocks of 128 queries, tiles of 128 keys, q-head pairs per kv head
+  FastDiv div_qblk, div_pairs, div_hk;
   float scale_log2;            // softmax scale * log2(e)
-  int64_t units;
+  int64_t units;               // < 2^31 (checked on the host)
   unsigned int* status;
 };
 
@@ -114,12 +134,14 @@ __device__ __forceinline__ int key_tile(const Unit& w, int i) {
 
 __device__ __forceinline__ Unit decode(const Params& p, int64_t u) {
   Unit w;
-  w.qb = (int)(u % p.n_qblk);
-  int64_t r = u / p.n_qblk;
-  const int pair = (int)(r % p.pairs);
-  r /= p.pairs;
-  w.hk = (int)(r % p.Hk);
-  w.b = (int)(r / p.Hk);
+  const uint32_t n = (uint32_t)u;  // u < units < 2^31
+  const uint32_t r1 = fast_div(n, p.div_qblk);
+  w.qb = (int)(n - r1 * p.div_qblk.d);
+  const uint32_t r2 = fast_div(r1, p.div_pairs);
+  const int pair = (int)(r1 - r2 * p.div_pairs.d);
+  const uint32_t r3 = fast_div(r2, p.div_hk);
+  w.hk = (int)(r2 - r3 * p.div_hk.d);
+  w.b = (int)r3;
   w.h0 = w.hk * p.G + 2 * pair;
   const int q0 = w.qb * kBlk;
   if (p.window >= 0) {
@@ -653,10 +675,14 @@ extern "C" int demon_attention(const DemonAttnArgs* a, void* stream) {
   p.pairs = p.G / 2;
   p.scale_log2 = (float)((double)a->scale * 1.4426950408889634);
   p.units = (int64_t)a->B * a->Hk * p.pairs * p.n_qblk;
+  DEMON_CHECK_ARG(p.units < ((int64_t)1 << 31), "attention: too many work units (%lld)", (long long)p.units);
+  p.div_qblk = attn::make_fastdiv((uint32_t)p.n_qblk);
+  p.div_pairs = attn::make_fastdiv((uint32_t)p.pairs);
+  p.div_hk = attn::make_fastdiv((uint32_t)p.Hk);
   p.status = status_word();
   if (device_pending(g_attn_attr)) {
-    // the warpgroups' register split adds up to exactly the launch's registers; with any
-    // other per-thread count at launch the softmax warps' setmaxnreg.inc would never return
+    // the warpgroups' register split is sized against the launch's 128 registers per thread;
+    // with fewer at launch the softmax warps' setmaxnreg.inc would never return
     cudaFuncAttributes fa;
     DEMON_CUDA(cudaFuncGetAttributes(&fa, attn::attention_kernel));
     if (fa.numRegs != attn::kLaunchRegs) {
