@@ -14,8 +14,8 @@
 // CTAs (one per SM) walk the units in a static round-robin; a band unit visits its diagonal
 // key tile first (rows then start from a running maximum over 128 keys).
 //
-// Warp roles (512 threads, four warpgroups; setmaxnreg moves registers from the issuing
-// warpgroup to the softmax warpgroups):
+// Warp roles (512 threads, four warpgroups; setmaxnreg moves registers from the epilogue and
+// issuing warpgroups to the softmax warpgroups):
 //   warpgroup 0 / 1  softmax of q head 0 / 1 of the unit, one query row per thread,
 //   warpgroup 2      epilogue: O_h / rowsum -> bf16 -> swizzled shared memory -> TMA store,
 //   warp 12          TMA loads: Q tiles into a 3-slot ring, K / V tiles into a 3-slot ring,
