@@ -348,7 +348,8 @@ DEMON_API int demon_ode_cluster_size(int32_t n_slots, int64_t T, int32_t* cluste
  * lines 110-112 of the same file, with the GQA K / V heads shared instead of repeated.
  * fp32 scores and softmax, bf16 probabilities into the P V product; each (sequence, head,
  * query block) is computed from that sequence alone (no split over keys), so results do
- * not depend on the batch.
+ * not depend on the batch.  Limits (DEMON_ERR_INVALID otherwise): S, L < 2^30 and
+ * B * Hq / 2 * ceil(S / 128) < 2^31 work units.
  */
 typedef struct DemonAttnArgs {
   const void* q;
